@@ -1,0 +1,155 @@
+/*
+ * sm100_fp8_wgrad.h -- C ABI of the B200 (sm_100a) grouped FP8 Wgrad engine.
+ *
+ * The engine computes, for every expert e of a sparse MoE layer,
+ *
+ *   out[e, m, n] = sum_{b in blocks(e)} sum_{k in b}
+ *                    lhs_q[k, m] * lhs_s[b, m] * rhs_q[k, n] * rhs_s[b, n]
+ *
+ * where the contraction index k runs over the expert's token rows, grouped in
+ * 128-row scale blocks b, lhs_q / rhs_q are FP8 e4m3 and lhs_s / rhs_s are fp32.
+ * The two MoE weight gradients are two calls:
+ *   dW_down[e]    = grad_y_e^T       @ hidden_e   (lhs = grad_y,       rhs = hidden)
+ *   dW_gate_up[e] = grad_gate_up_e^T @ x_e        (lhs = grad_gate_up, rhs = x)
+ *
+ * Everything here is plain C: device pointers, sizes and a CUDA stream passed
+ * as void*. Every entry point returns an int status (SM100_WGRAD_OK == 0) and
+ * never synchronises the stream. The caller owns and allocates all buffers.
+ *
+ * Memory layouts (identical to the reference operator contract):
+ *   FP8 operand data  : [cols][pitch] bytes, K (token rows) contiguous; the
+ *                       reference exposes it as a logical [K_rows, cols] view
+ *                       with stride (1, pitch). pitch % 16 == 0.
+ *   scales            : [total_blocks][cols] fp32, row-major.
+ *   out               : [E][M][N] bf16 or fp32, row-major (contiguous).
+ *   block_offsets     : [E+1] int32, prefix sum of ceil(rows_e / 128).
+ *   k_row_offsets     : [E+1] int32, first operand K row of each expert
+ *                       (padded layout: 128 * block_offsets).
+ */
+#ifndef SM100_FP8_WGRAD_H_
+#define SM100_FP8_WGRAD_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SM100_WGRAD_API __attribute__((visibility("default")))
+#else
+#define SM100_WGRAD_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status codes */
+#define SM100_WGRAD_OK 0
+#define SM100_WGRAD_ERR_INVALID_ARG 1      /* null pointer, bad size, bad stride or alignment */
+#define SM100_WGRAD_ERR_UNSUPPORTED_ARCH 2 /* device is not compute capability 10.0 (B200)    */
+#define SM100_WGRAD_ERR_LAUNCH 3           /* CUDA launch / attribute / driver call failed   */
+#define SM100_WGRAD_ERR_TENSOR_MAP 4       /* cuTensorMapEncodeTiled rejected a descriptor   */
+#define SM100_WGRAD_ERR_DEVICE_TIMEOUT 5   /* a device-side bounded wait expired             */
+#define SM100_WGRAD_ERR_UNSUPPORTED 6      /* shape or option outside the supported envelope */
+
+#define SM100_WGRAD_OUT_BF16 0
+#define SM100_WGRAD_OUT_F32 1
+
+/* Tile configurations selectable through Sm100WgradArgs.tile_config. */
+#define SM100_WGRAD_TILE_AUTO 0
+#define SM100_WGRAD_TILE_128x256 1
+#define SM100_WGRAD_TILE_128x128 2
+
+typedef struct Sm100WgradArgs {
+  const void* lhs_data;      /* FP8 e4m3 [M][lhs_pitch]                              */
+  int64_t lhs_pitch;         /* bytes between consecutive columns (m) of lhs        */
+  const float* lhs_scales;   /* [total_blocks][M]                                    */
+  const void* rhs_data;      /* FP8 e4m3 [N][rhs_pitch]                              */
+  int64_t rhs_pitch;         /* bytes between consecutive columns (n) of rhs        */
+  const float* rhs_scales;   /* [total_blocks][N]                                    */
+  void* out;                 /* [E][M][N]                                            */
+  int32_t out_dtype;         /* SM100_WGRAD_OUT_BF16 or SM100_WGRAD_OUT_F32          */
+  int32_t accumulate;        /* 0: out = result, 1: out += result                    */
+  int64_t num_experts;       /* E                                                    */
+  int64_t m;                 /* M (lhs columns)                                      */
+  int64_t n;                 /* N (rhs columns)                                      */
+  int64_t k_rows;            /* operand K extent (padded rows)                       */
+  int64_t total_blocks;      /* number of 128-row scale blocks                       */
+  const int32_t* block_offsets;  /* device [E+1]                                     */
+  const int32_t* k_row_offsets;  /* device [E+1]                                     */
+  const int32_t* expert_order;   /* device [E] schedule order (LPT), or NULL = 0..E-1 */
+  int32_t tile_config;       /* SM100_WGRAD_TILE_*                                   */
+  int32_t max_ctas;          /* persistent grid cap, 0 = one CTA per SM              */
+} Sm100WgradArgs;
+
+/*
+ * Grouped FP8 Wgrad GEMM (one launch of the persistent tcgen05 kernel).
+ * Replaces fp8_grouped_wgrad_sm90_impl, src/sm90_fp8_wgrad/gemm_sm90.py:5526-5899
+ * (the TVM-FFI launch of the CuTe-DSL kernel at gemm_sm90.py:5886), called from
+ * fp8_grouped_wgrad_sm90, src/sm90_fp8_wgrad/interface.py:243-255.
+ * Unlike the reference (gemm_sm90.py:5676) it performs no device->host read.
+ */
+SM100_WGRAD_API int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* args, void* stream);
+
+/*
+ * 1x128 FP8 quantiser: per (128-row block b, column c)
+ *   amax = max_{k < row_count[b]} |x[row_start[b] + k, c]|
+ *   scale[b, c] = max(amax / 448, 1e-12)
+ *   q[c][128 b + k] = e4m3_rne_satfinite(x / scale)  (0 for k >= row_count[b])
+ * x is BF16 (x_dtype 0) or fp32 (x_dtype 1) row-major [valid_rows][cols].
+ * Replaces the Triton kernel _quantize_grouped_wgrad_128x1_kernel,
+ * src/sm90_fp8_wgrad/quant.py:105-167, launched from
+ * quantize_grouped_wgrad_operand_128x1, quant.py:175-270 (padded layout).
+ */
+SM100_WGRAD_API int sm100_wgrad_quantize_1x128(const void* x, int32_t x_dtype, int64_t valid_rows, int64_t cols,
+                               const int32_t* block_row_start, const int32_t* block_row_count,
+                               int64_t total_blocks, void* q_data, int64_t q_pitch, float* scales,
+                               void* stream);
+
+/*
+ * Scale-block metadata builder (device side, no host sync).
+ * From cu_seqlens_k [E+1] it writes the per-expert arrays
+ *   blocks_per_expert[E], block_offsets[E+1], padded_cu_seqlens_k[E+1],
+ *   wgmma_cu_seqlens_k[E+1] (32-row aligned), tail_valid_rows[E],
+ *   tail_wgmma_atoms[E], tail_copy_k[E], has_tail[E] (uint8), expert_order[E]
+ * and the per-block arrays (capacity block_capacity entries)
+ *   block_row_start, block_row_count, wgmma_block_row_start
+ * plus totals[5] = {valid_rows, padded_rows, wgmma_rows, total_blocks, status}
+ * (status != 0 means cu_seqlens_k was not monotonic or block_capacity was too
+ * small). Replaces build_wgrad_scale_block_meta,
+ * src/sm90_fp8_wgrad/block_meta.py:252-349 (CPU loops at :288-294).
+ */
+typedef struct Sm100WgradMetaOut {
+  int32_t* blocks_per_expert;
+  int32_t* block_offsets;
+  int32_t* padded_cu_seqlens_k;
+  int32_t* wgmma_cu_seqlens_k;
+  int32_t* tail_valid_rows;
+  int32_t* tail_wgmma_atoms;
+  int32_t* tail_copy_k;
+  uint8_t* has_tail;
+  int32_t* expert_order;
+  int32_t* block_row_start;
+  int32_t* block_row_count;
+  int32_t* wgmma_block_row_start;
+  int64_t block_capacity;
+  int64_t* totals;
+} Sm100WgradMetaOut;
+
+SM100_WGRAD_API int sm100_wgrad_build_meta(const int32_t* cu_seqlens_k, int64_t num_experts, const Sm100WgradMetaOut* out,
+                           void* stream);
+
+/* Reads and clears the device error word of the current device (synchronous;
+ * diagnostics only, never call it inside a timed region). Writes one of the
+ * device error codes (0 = none) to *code. */
+SM100_WGRAD_API int sm100_wgrad_device_error(int32_t* code);
+
+/* Human-readable text of a status code (static storage). */
+SM100_WGRAD_API const char* sm100_wgrad_status_string(int status);
+
+/* Library version, e.g. "0.1.0". */
+SM100_WGRAD_API const char* sm100_wgrad_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SM100_FP8_WGRAD_H_ */

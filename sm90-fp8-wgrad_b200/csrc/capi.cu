@@ -1,0 +1,258 @@
+// C-ABI entry points of the grouped FP8 Wgrad engine (declared in
+// include/sm100_fp8_wgrad.h). Host-side argument validation, TMA descriptor
+// encoding and kernel launch; no entry point synchronises the stream.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "../../include/sm100_fp8_wgrad.h"
+#include "ptx.cuh"
+#include "wgrad_gemm.cuh"
+
+namespace wgrad {
+cudaError_t launch_quantize_1x128(const void* x, int x_dtype, int64_t cols, const int32_t* block_row_start,
+                                  const int32_t* block_row_count, int64_t total_blocks, void* q, int64_t q_pitch,
+                                  float* scales, cudaStream_t stream);
+cudaError_t launch_build_meta(const int32_t* cu, int64_t num_experts, const Sm100WgradMetaOut& out,
+                              cudaStream_t stream);
+}  // namespace wgrad
+
+namespace {
+
+using wgrad::GemmParams;
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+  });
+  return fn;
+}
+
+// Per-device capability check and SM count, cached.
+struct DeviceInfo {
+  int sm_count = 0;
+  int major = 0;
+  int minor = 0;
+};
+
+int device_info(DeviceInfo* info) {
+  static std::mutex mu;
+  static DeviceInfo cache[64];
+  static bool have[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SM100_WGRAD_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 0 || dev >= 64) return SM100_WGRAD_ERR_LAUNCH;
+  if (!have[dev]) {
+    DeviceInfo d;
+    if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+      return SM100_WGRAD_ERR_LAUNCH;
+    cache[dev] = d;
+    have[dev] = true;
+  }
+  *info = cache[dev];
+  return SM100_WGRAD_OK;
+}
+
+int check_arch(DeviceInfo* info) {
+  const int st = device_info(info);
+  if (st != SM100_WGRAD_OK) return st;
+  // sm_100a code runs on compute capability 10.0 only.
+  if (info->major != 10 || info->minor != 0) return SM100_WGRAD_ERR_UNSUPPORTED_ARCH;
+  return SM100_WGRAD_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// FP8 operand [cols][pitch] bytes, box = 128 K-bytes x box_rows columns, 128B swizzle.
+int encode_operand_map(CUtensorMap* map, const void* data, int64_t k_rows, int64_t cols, int64_t pitch,
+                       int box_rows) {
+  auto encode = get_encode_fn();
+  if (encode == nullptr) return SM100_WGRAD_ERR_LAUNCH;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k_rows), static_cast<cuuint64_t>(cols)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
+  const cuuint32_t box[2] = {128u, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(data), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SM100_WGRAD_OK : SM100_WGRAD_ERR_TENSOR_MAP;
+}
+
+// Output [E][M][N]; box = (64 bf16 | 32 fp32) columns x 32 rows x 1 expert, 128B swizzle.
+int encode_out_map(CUtensorMap* map, void* out, int out_f32, int64_t e, int64_t m, int64_t n) {
+  auto encode = get_encode_fn();
+  if (encode == nullptr) return SM100_WGRAD_ERR_LAUNCH;
+  const int64_t esz = out_f32 ? 4 : 2;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m), static_cast<cuuint64_t>(e)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(n * esz), static_cast<cuuint64_t>(m * n * esz)};
+  const cuuint32_t box[3] = {out_f32 ? 32u : 64u, 32u, 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUresult r =
+      encode(map, out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dims, strides,
+             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SM100_WGRAD_OK : SM100_WGRAD_ERR_TENSOR_MAP;
+}
+
+int pick_bn(int32_t tile_config, int64_t n) {
+  if (tile_config == SM100_WGRAD_TILE_128x128) return 128;
+  if (tile_config == SM100_WGRAD_TILE_128x256) return 256;
+  // auto: the wide tile halves operand re-reads per output byte; a narrow N
+  // would only fill it with zero columns.
+  return n <= 128 ? 128 : 256;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* sm100_wgrad_version(void) { return "0.1.0"; }
+
+const char* sm100_wgrad_status_string(int status) {
+  switch (status) {
+    case SM100_WGRAD_OK: return "ok";
+    case SM100_WGRAD_ERR_INVALID_ARG: return "invalid argument";
+    case SM100_WGRAD_ERR_UNSUPPORTED_ARCH: return "unsupported GPU architecture (requires sm_100a / B200)";
+    case SM100_WGRAD_ERR_LAUNCH: return "CUDA launch or driver call failed";
+    case SM100_WGRAD_ERR_TENSOR_MAP: return "TMA descriptor encoding failed";
+    case SM100_WGRAD_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case SM100_WGRAD_ERR_UNSUPPORTED: return "unsupported shape or option";
+    default: return "unknown status";
+  }
+}
+
+int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
+  if (a == nullptr) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->out == nullptr || a->block_offsets == nullptr || a->k_row_offsets == nullptr) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->num_experts < 0 || a->m <= 0 || a->n <= 0 || a->k_rows < 0 || a->total_blocks < 0)
+    return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->out_dtype != SM100_WGRAD_OUT_BF16 && a->out_dtype != SM100_WGRAD_OUT_F32) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->tile_config != SM100_WGRAD_TILE_AUTO && a->tile_config != SM100_WGRAD_TILE_128x256 &&
+      a->tile_config != SM100_WGRAD_TILE_128x128)
+    return SM100_WGRAD_ERR_INVALID_ARG;
+  // TMA: output row pitch and scale-vector chunks must be 16-byte multiples.
+  if (a->m % 16 != 0 || a->n % 16 != 0) return SM100_WGRAD_ERR_UNSUPPORTED;
+  if (a->m > (1 << 30) || a->n > (1 << 30) || a->num_experts > (1 << 30)) return SM100_WGRAD_ERR_UNSUPPORTED;
+  if (!aligned16(a->out)) return SM100_WGRAD_ERR_INVALID_ARG;
+  const bool has_operands = a->k_rows > 0 && a->total_blocks > 0;
+  if (has_operands) {
+    if (a->lhs_data == nullptr || a->rhs_data == nullptr || a->lhs_scales == nullptr || a->rhs_scales == nullptr)
+      return SM100_WGRAD_ERR_INVALID_ARG;
+    if (a->lhs_pitch % 16 != 0 || a->rhs_pitch % 16 != 0 || a->lhs_pitch < a->k_rows || a->rhs_pitch < a->k_rows)
+      return SM100_WGRAD_ERR_INVALID_ARG;
+    if (a->k_rows % 128 != 0) return SM100_WGRAD_ERR_UNSUPPORTED;  // padded layout: whole 128-row blocks
+    if (!aligned16(a->lhs_data) || !aligned16(a->rhs_data) || !aligned16(a->lhs_scales) ||
+        !aligned16(a->rhs_scales))
+      return SM100_WGRAD_ERR_INVALID_ARG;
+  }
+  if (a->num_experts == 0) return SM100_WGRAD_OK;
+
+  DeviceInfo info;
+  int st = check_arch(&info);
+  if (st != SM100_WGRAD_OK) return st;
+
+  const int bn = pick_bn(a->tile_config, a->n);
+  CUtensorMap ta{}, tb{}, to{};
+  if (has_operands) {
+    st = encode_operand_map(&ta, a->lhs_data, a->k_rows, a->m, a->lhs_pitch, 128);
+    if (st != SM100_WGRAD_OK) return st;
+    st = encode_operand_map(&tb, a->rhs_data, a->k_rows, a->n, a->rhs_pitch, bn);
+    if (st != SM100_WGRAD_OK) return st;
+  }
+  st = encode_out_map(&to, a->out, a->out_dtype == SM100_WGRAD_OUT_F32, a->num_experts, a->m, a->n);
+  if (st != SM100_WGRAD_OK) return st;
+
+  GemmParams p{};
+  p.sa = a->lhs_scales;
+  p.sb = a->rhs_scales;
+  p.out = a->out;
+  p.block_offsets = a->block_offsets;
+  p.k_row_offsets = a->k_row_offsets;
+  p.expert_order = a->expert_order;
+  p.num_experts = static_cast<int>(a->num_experts);
+  p.m = static_cast<int>(a->m);
+  p.n = static_cast<int>(a->n);
+  p.bn = bn;
+  p.tiles_n = static_cast<int>((a->n + bn - 1) / bn);
+  const int64_t tiles_m = (a->m + 127) / 128;
+  const int64_t tpe = tiles_m * p.tiles_n;
+  const int64_t num_tiles = tpe * a->num_experts;
+  if (num_tiles > INT32_MAX) return SM100_WGRAD_ERR_UNSUPPORTED;
+  p.tiles_per_expert = static_cast<int>(tpe);
+  p.num_tiles = static_cast<int>(num_tiles);
+  p.out_f32 = a->out_dtype == SM100_WGRAD_OUT_F32;
+  p.accumulate = a->accumulate != 0;
+  p.has_operands = has_operands ? 1 : 0;
+
+  int grid = info.sm_count;
+  if (a->max_ctas > 0 && a->max_ctas < grid) grid = a->max_ctas;
+  if (num_tiles < grid) grid = static_cast<int>(num_tiles);
+  const cudaError_t err = wgrad::launch_grouped_wgrad(ta, tb, to, p, grid, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? SM100_WGRAD_OK : SM100_WGRAD_ERR_LAUNCH;
+}
+
+int sm100_wgrad_quantize_1x128(const void* x, int32_t x_dtype, int64_t valid_rows, int64_t cols,
+                               const int32_t* block_row_start, const int32_t* block_row_count,
+                               int64_t total_blocks, void* q_data, int64_t q_pitch, float* scales, void* stream) {
+  if (x_dtype != 0 && x_dtype != 1) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (valid_rows < 0 || cols < 0 || total_blocks < 0) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (total_blocks == 0 || cols == 0) return SM100_WGRAD_OK;
+  if (x == nullptr && valid_rows > 0) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (block_row_start == nullptr || block_row_count == nullptr || q_data == nullptr || scales == nullptr)
+    return SM100_WGRAD_ERR_INVALID_ARG;
+  if (q_pitch % 16 != 0 || q_pitch < total_blocks * 128 || !aligned16(q_data)) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (total_blocks > INT32_MAX) return SM100_WGRAD_ERR_UNSUPPORTED;
+  DeviceInfo info;
+  const int st = check_arch(&info);
+  if (st != SM100_WGRAD_OK) return st;
+  const cudaError_t err = wgrad::launch_quantize_1x128(x, x_dtype, cols, block_row_start, block_row_count,
+                                                       total_blocks, q_data, q_pitch, scales,
+                                                       static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? SM100_WGRAD_OK : SM100_WGRAD_ERR_LAUNCH;
+}
+
+int sm100_wgrad_build_meta(const int32_t* cu_seqlens_k, int64_t num_experts, const Sm100WgradMetaOut* out,
+                           void* stream) {
+  if (cu_seqlens_k == nullptr || out == nullptr || num_experts < 0) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (out->totals == nullptr || out->block_offsets == nullptr || out->padded_cu_seqlens_k == nullptr ||
+      out->wgmma_cu_seqlens_k == nullptr || out->expert_order == nullptr ||
+      (num_experts > 0 && (out->blocks_per_expert == nullptr || out->tail_valid_rows == nullptr ||
+                           out->tail_wgmma_atoms == nullptr || out->tail_copy_k == nullptr ||
+                           out->has_tail == nullptr)) ||
+      out->block_capacity < 0)
+    return SM100_WGRAD_ERR_INVALID_ARG;
+  if (out->block_capacity > 0 &&
+      (out->block_row_start == nullptr || out->block_row_count == nullptr || out->wgmma_block_row_start == nullptr))
+    return SM100_WGRAD_ERR_INVALID_ARG;
+  DeviceInfo info;
+  const int st = check_arch(&info);
+  if (st != SM100_WGRAD_OK) return st;
+  const cudaError_t err = wgrad::launch_build_meta(cu_seqlens_k, num_experts, *out, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? SM100_WGRAD_OK : SM100_WGRAD_ERR_LAUNCH;
+}
+
+int sm100_wgrad_device_error(int32_t* code) {
+  if (code == nullptr) return SM100_WGRAD_ERR_INVALID_ARG;
+  unsigned int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, wgrad::g_device_error, sizeof(v)) != cudaSuccess) return SM100_WGRAD_ERR_LAUNCH;
+  if (v != 0 && cudaMemcpyToSymbol(wgrad::g_device_error, &zero, sizeof(zero)) != cudaSuccess)
+    return SM100_WGRAD_ERR_LAUNCH;
+  *code = static_cast<int32_t>(v);
+  return SM100_WGRAD_OK;
+}
+
+}  // extern "C"

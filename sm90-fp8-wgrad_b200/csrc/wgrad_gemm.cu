@@ -1,0 +1,400 @@
+// Persistent, warp-specialised grouped FP8 Wgrad GEMM for sm_100a (B200).
+//
+// Computes, per expert e and output tile (m0, n0):
+//   out[e, m, n] = sum_b  sa[b, m] * sb[b, n] * ( sum_{k in b} A[m, k] * B[n, k] )
+// with A = lhs FP8 [M][pitch] and B = rhs FP8 [N][pitch] (K contiguous), b the
+// expert's 128-row scale blocks. This is the math of the reference kernel
+// Fp8ScaledWgradSm90 (src/sm90_fp8_wgrad/gemm_sm90.py:1211-2321): a fresh
+// tensor-core partial per 128-row K block (mma_scaled_128k, :3910-4105),
+// promoted into an fp32 accumulator with the rank-1 scale product
+// (promote_scaled_acc_epilogue_staged, :5023-5085), converted to BF16 in the
+// epilogue (:2211-2290).
+//
+// B200 design (not a translation of the SM90 kernel):
+//   warp 0      : TMA producer. A/B tiles (128 x 128 B, BN x 128 B, 128B
+//                 swizzle) into a STAGES-deep shared-memory ring; the per-block
+//                 scale vectors sa[128], sb[BN] via 1-D bulk copies into a
+//                 separate SCALE_STAGES-deep ring.
+//   warp 1      : MMA issuer. One elected lane issues 4 x tcgen05.mma
+//                 (kind::f8f6f4, 128 x BN x 32) per K block into one of two
+//                 TMEM partial buffers, then tcgen05.commit frees the smem
+//                 stage and signals the partial as ready.
+//   warps 2, 3  : idle (complete warpgroup 0, which gives registers away).
+//   warps 4..11 : promotion + epilogue. tcgen05.ld the partial (thread = TMEM
+//                 lane = output row), final += (raw * sb[n]) * sa[m] with packed
+//                 f32x2 FMA, release the TMEM buffer so the tensor pipe
+//                 computes block b+1 while block b is promoted. At tile end:
+//                 fp32 -> BF16 (or fp32), swizzled smem staging, TMA store.
+// The serialised WGMMA -> wait -> promote chain of the SM90 kernel
+// (gemm_sm90.py:3945, 4023) becomes a two-deep TMEM pipeline here.
+//
+// Tile schedule: static persistent round robin over
+//   tile t -> (expert_order[t / tiles_per_expert], m_tile, n_tile)
+// with n fastest; expert_order is LPT (most K blocks first) when supplied.
+// Experts with no rows still produce their (zero) tiles, as the reference
+// does (gemm_sm90.py:3933).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "ptx.cuh"
+#include "wgrad_gemm.cuh"
+
+namespace wgrad {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 128;  // scale block == K block, bytes per row of an FP8 tile
+constexpr int STAGES = 3;
+constexpr int SCALE_STAGES = 6;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int NUM_THREADS = 32 * (4 + NUM_EPI_WARPS);  // warpgroup 0: TMA, MMA, 2 idle; warpgroups 1-2: epilogue
+constexpr int FIRST_EPI_WARP = 4;
+// Register split (launch: 65536 / 384 = 168 per thread): 128 x 56 + 256 x 224 = 64512.
+constexpr uint32_t REGS_CONTROL = 56;
+constexpr uint32_t REGS_EPILOGUE = 224;
+constexpr int OUT_STAGE_BYTES_PER_WARP = 8192;
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int SCALE_FLOATS = BM + BN;
+  static constexpr int COLS_PER_WARP = BN / 2;     // two column halves of 4 warps each
+  static constexpr int CHUNKS = COLS_PER_WARP / 16;  // tcgen05.ld x16 chunks
+  static constexpr int TMEM_COLS = 2 * BN;          // double-buffered partial
+  static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + NUM_EPI_WARPS * OUT_STAGE_BYTES_PER_WARP +
+                                    SCALE_STAGES * SCALE_FLOATS * 4 + 256 /*barriers*/ + 1024 /*align*/;
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+struct TileCoord {
+  int e, m0, n0;
+};
+
+__device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, int tile) {
+  const int e_slot = tile / p.tiles_per_expert;
+  const int local = tile - e_slot * p.tiles_per_expert;
+  const int tm = local / p.tiles_n;
+  const int tn = local - tm * p.tiles_n;
+  TileCoord c;
+  c.e = p.expert_order != nullptr ? __ldg(p.expert_order + e_slot) : e_slot;
+  c.m0 = tm * BM;
+  c.n0 = tn * p.bn;
+  return c;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    grouped_wgrad_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                         const __grid_constant__ CUtensorMap tmap_out, const GemmParams p) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_a = smem;
+  uint8_t* s_b = s_a + STAGES * C::A_BYTES;
+  uint8_t* s_out = s_b + STAGES * C::B_BYTES;
+  float* s_scale = reinterpret_cast<float*>(s_out + NUM_EPI_WARPS * OUT_STAGE_BYTES_PER_WARP);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_scale + SCALE_STAGES * C::SCALE_FLOATS);
+  uint64_t* full_bar = bars;                          // [STAGES]   TMA -> MMA
+  uint64_t* empty_bar = full_bar + STAGES;            // [STAGES]   MMA -> TMA
+  uint64_t* sfull_bar = empty_bar + STAGES;           // [SCALE_STAGES] TMA -> epilogue
+  uint64_t* sempty_bar = sfull_bar + SCALE_STAGES;    // [SCALE_STAGES] epilogue -> TMA
+  uint64_t* tfull_bar = sempty_bar + SCALE_STAGES;    // [2] MMA -> epilogue
+  uint64_t* tempty_bar = tfull_bar + 2;               // [2] epilogue -> MMA
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < SCALE_STAGES; ++i) {
+      mbar_init(&sfull_bar[i], 1);
+      mbar_init(&sempty_bar[i], NUM_EPI_WARPS);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], NUM_EPI_WARPS);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0 && p.has_operands) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+    tma_prefetch_desc(&tmap_out);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp < FIRST_EPI_WARP) setmaxnreg_dec<REGS_CONTROL>();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0, sstage = 0;
+      uint32_t phase = 0, sphase = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+        const TileCoord tc = decode_tile(p, tile);
+        const int kb0 = __ldg(p.block_offsets + tc.e);
+        const int nkb = __ldg(p.block_offsets + tc.e + 1) - kb0;
+        const int krow0 = __ldg(p.k_row_offsets + tc.e);
+        const uint32_t a_scale_bytes = static_cast<uint32_t>(min(BM, p.m - tc.m0)) * 4u;
+        const uint32_t b_scale_bytes = static_cast<uint32_t>(min(BN, p.n - tc.n0)) * 4u;
+        bool ok = true;
+        for (int kb = 0; kb < nkb && ok; ++kb) {
+          ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, kDevTimeoutProducer);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&full_bar[stage], C::A_BYTES + C::B_BYTES);
+          tma_load_2d(s_a + stage * C::A_BYTES, &tmap_a, &full_bar[stage], krow0 + kb * BK, tc.m0);
+          tma_load_2d(s_b + stage * C::B_BYTES, &tmap_b, &full_bar[stage], krow0 + kb * BK, tc.n0);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+
+          ok = mbar_wait(&sempty_bar[sstage], sphase ^ 1u, abort_flag, kDevTimeoutProducer);
+          if (!ok) break;
+          float* dst = s_scale + sstage * C::SCALE_FLOATS;
+          const size_t blk = static_cast<size_t>(kb0 + kb);
+          mbar_arrive_expect_tx(&sfull_bar[sstage], a_scale_bytes + b_scale_bytes);
+          bulk_load_1d(dst, p.sa + blk * p.m + tc.m0, a_scale_bytes, &sfull_bar[sstage]);
+          bulk_load_1d(dst + BM, p.sb + blk * p.n + tc.n0, b_scale_bytes, &sfull_bar[sstage]);
+          if (++sstage == SCALE_STAGES) { sstage = 0; sphase ^= 1u; }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = umma_idesc_e4m3_f32(BM, BN);
+    int stage = 0, acc = 0;
+    uint32_t phase = 0, aphase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      const TileCoord tc = decode_tile(p, tile);
+      const int nkb = __ldg(p.block_offsets + tc.e + 1) - __ldg(p.block_offsets + tc.e);
+      for (int kb = 0; kb < nkb; ++kb) {
+        // Whole warp waits (keeps the warp converged for the .sync.aligned ops).
+        ok = mbar_wait(&tempty_bar[acc], aphase ^ 1u, abort_flag, kDevTimeoutMma);
+        if (ok) ok = mbar_wait(&full_bar[stage], phase, abort_flag, kDevTimeoutMma);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_addr = smem_u32(s_a + stage * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(s_b + stage * C::B_BYTES);
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            // advance 32 bytes (one K=32 FP8 slice) inside the 128-byte swizzle atom
+            umma_f8(d_tmem, umma_desc_k_sw128(a_addr + k * 32), umma_desc_k_sw128(b_addr + k * 32), idesc,
+                    k > 0 ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          umma_commit(&tfull_bar[acc]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        acc ^= 1;
+        if (acc == 0) aphase ^= 1u;
+      }
+    }
+  } else if (warp >= FIRST_EPI_WARP) {
+    // ------------------------------------------------------------ promotion + epilogue
+    setmaxnreg_inc<REGS_EPILOGUE>();
+    const int ew = warp - FIRST_EPI_WARP;    // 0..7
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int half = ew >> 2;                // column half of the tile
+    const int row = quarter * 32 + lane;     // row within the tile == TMEM lane
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    uint8_t* stage_out = s_out + ew * OUT_STAGE_BYTES_PER_WARP;
+    const uint32_t stage_out_addr = smem_u32(stage_out);
+
+    int acc = 0, sstage = 0;
+    uint32_t aphase = 0, sphase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      const TileCoord tc = decode_tile(p, tile);
+      const int nkb = __ldg(p.block_offsets + tc.e + 1) - __ldg(p.block_offsets + tc.e);
+      float fin[C::COLS_PER_WARP];
+#pragma unroll
+      for (int j = 0; j < C::COLS_PER_WARP; ++j) fin[j] = 0.f;
+
+      for (int kb = 0; kb < nkb; ++kb) {
+        ok = mbar_wait(&tfull_bar[acc], aphase, abort_flag, kDevTimeoutEpilogue);
+        if (ok) ok = mbar_wait(&sfull_bar[sstage], sphase, abort_flag, kDevTimeoutEpilogue);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const float* sc = s_scale + sstage * C::SCALE_FLOATS;
+        const float a_s = sc[row];
+        const float* b_s = sc + BM + half * C::COLS_PER_WARP;
+        const uint32_t t_addr = tmem_base + lane_addr + static_cast<uint32_t>(acc * BN + half * C::COLS_PER_WARP);
+#pragma unroll
+        for (int c = 0; c < C::CHUNKS; ++c) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(t_addr + c * 16, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            const float4 sb4 = *reinterpret_cast<const float4*>(b_s + c * 16 + j);
+            float u0, u1, u2, u3;
+            mul_f32x2(u0, u1, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), sb4.x, sb4.y);
+            mul_f32x2(u2, u3, __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]), sb4.z, sb4.w);
+            float* f = &fin[c * 16 + j];
+            fma_f32x2(f[0], f[1], u0, u1, a_s, a_s, f[0], f[1]);
+            fma_f32x2(f[2], f[3], u2, u3, a_s, a_s, f[2], f[3]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&tempty_bar[acc]);
+          mbar_arrive(&sempty_bar[sstage]);
+        }
+        acc ^= 1;
+        if (acc == 0) aphase ^= 1u;
+        if (++sstage == SCALE_STAGES) { sstage = 0; sphase ^= 1u; }
+      }
+      if (!ok) break;
+
+      // -------------------------------------------------------- epilogue store
+      const int g_row = tc.m0 + row;
+      const int col0 = tc.n0 + half * C::COLS_PER_WARP;
+      if (p.accumulate) {
+        const bool row_ok = g_row < p.m;
+        const size_t base = (static_cast<size_t>(tc.e) * p.m + (row_ok ? g_row : 0)) * p.n;
+#pragma unroll
+        for (int j = 0; j < C::COLS_PER_WARP; ++j) {
+          const int gc = col0 + j;
+          if (row_ok && gc < p.n) {
+            fin[j] += p.out_f32 ? reinterpret_cast<const float*>(p.out)[base + gc]
+                                : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.out)[base + gc]);
+          }
+        }
+      }
+      // The previous tile's TMA store must have finished reading the staging buffer.
+      if (lane == 0) bulk_wait_group_read0();
+      __syncwarp();
+      const bool rows_in = (tc.m0 + quarter * 32) < p.m;
+      const uint32_t swz = static_cast<uint32_t>(lane & 7);
+      if (!p.out_f32) {
+        // bf16: boxes of 32 rows x 64 columns (128 B rows, 128B swizzle), 4 KB each.
+        constexpr int BOXES = C::COLS_PER_WARP / 64;
+#pragma unroll
+        for (int bx = 0; bx < BOXES; ++bx) {
+          const uint32_t box = stage_out_addr + bx * 4096 + lane * 128;
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            const float* v = &fin[bx * 64 + ch * 8];
+            st_shared_v4(box + ((ch ^ swz) << 4), pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                         pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && rows_in) {
+#pragma unroll
+          for (int bx = 0; bx < BOXES; ++bx) {
+            const int c = col0 + bx * 64;
+            if (c < p.n) tma_store_3d(&tmap_out, stage_out + bx * 4096, c, tc.m0 + quarter * 32, tc.e);
+          }
+          bulk_commit_group();
+        }
+      } else {
+        // fp32: boxes of 32 rows x 32 columns, two boxes per staging round.
+        constexpr int BOXES = C::COLS_PER_WARP / 32;
+#pragma unroll
+        for (int bx0 = 0; bx0 < BOXES; bx0 += 2) {
+          if (bx0 > 0) {
+            if (lane == 0) bulk_wait_group_read0();
+            __syncwarp();
+          }
+#pragma unroll
+          for (int bi = 0; bi < 2; ++bi) {
+            const uint32_t box = stage_out_addr + bi * 4096 + lane * 128;
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+              const float* v = &fin[(bx0 + bi) * 32 + ch * 4];
+              st_shared_v4(box + ((ch ^ swz) << 4), __float_as_uint(v[0]), __float_as_uint(v[1]),
+                           __float_as_uint(v[2]), __float_as_uint(v[3]));
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && rows_in) {
+#pragma unroll
+            for (int bi = 0; bi < 2; ++bi) {
+              const int c = col0 + (bx0 + bi) * 32;
+              if (c < p.n) tma_store_3d(&tmap_out, stage_out + bi * 4096, c, tc.m0 + quarter * 32, tc.e);
+            }
+            bulk_commit_group();
+          }
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_group0();  // all output writes complete before exit
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+template <int BN>
+static cudaError_t launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                               const GemmParams& p, int grid, cudaStream_t stream) {
+  using C = Cfg<BN>;
+  static int configured_device_mask = 0;  // bit per device ordinal (< 32)
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 32 && !(configured_device_mask & (1 << dev))) {
+    err = cudaFuncSetAttribute(grouped_wgrad_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               C::SMEM_BYTES);
+    if (err != cudaSuccess) return err;
+    configured_device_mask |= (1 << dev);
+  } else if (dev >= 32) {
+    err = cudaFuncSetAttribute(grouped_wgrad_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               C::SMEM_BYTES);
+    if (err != cudaSuccess) return err;
+  }
+  grouped_wgrad_kernel<BN><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ta, tb, to, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_grouped_wgrad(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                                 const GemmParams& p, int grid, cudaStream_t stream) {
+  if (p.bn == 256) return launch_impl<256>(ta, tb, to, p, grid, stream);
+  return launch_impl<128>(ta, tb, to, p, grid, stream);
+}
+
+int smem_bytes_for_bn(int bn) { return bn == 256 ? Cfg<256>::SMEM_BYTES : Cfg<128>::SMEM_BYTES; }
+
+}  // namespace wgrad

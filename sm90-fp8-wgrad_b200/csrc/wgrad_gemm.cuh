@@ -1,0 +1,34 @@
+// Launch parameters shared by the grouped Wgrad kernel and its host launcher.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace wgrad {
+
+struct GemmParams {
+  const float* sa;              // lhs scales [total_blocks][m]
+  const float* sb;              // rhs scales [total_blocks][n]
+  void* out;                    // [E][m][n]
+  const int32_t* block_offsets; // [E+1]
+  const int32_t* k_row_offsets; // [E+1]
+  const int32_t* expert_order;  // [E] or nullptr
+  int num_experts;
+  int m, n;
+  int bn;                       // tile N (128 or 256); tile M is 128
+  int tiles_n;
+  int tiles_per_expert;
+  int num_tiles;
+  int out_f32;
+  int accumulate;
+  int has_operands;             // 0 when the operand K extent is empty
+};
+
+cudaError_t launch_grouped_wgrad(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                                 const GemmParams& p, int grid, cudaStream_t stream);
+
+int smem_bytes_for_bn(int bn);
+
+}  // namespace wgrad

@@ -1,0 +1,155 @@
+"""ctypes binding of the C-ABI library ``libsm100_fp8_wgrad.so``.
+
+The library (built from ``csrc/`` for sm_100a by ``build_ext.py``) is the only
+compute path of this package: there is no Python, PyTorch or CPU fallback. A
+missing or unloadable library raises ``RuntimeError`` at first use.
+
+The structures below mirror ``include/sm100_fp8_wgrad.h`` field by field.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+LIB_NAME = "libsm100_fp8_wgrad.so"
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / LIB_NAME
+
+OK = 0
+ERR_INVALID_ARG = 1
+ERR_UNSUPPORTED_ARCH = 2
+ERR_LAUNCH = 3
+ERR_TENSOR_MAP = 4
+ERR_DEVICE_TIMEOUT = 5
+ERR_UNSUPPORTED = 6
+
+OUT_BF16 = 0
+OUT_F32 = 1
+
+TILE_AUTO = 0
+TILE_128x256 = 1
+TILE_128x128 = 2
+
+# Every symbol include/sm100_fp8_wgrad.h declares.
+EXPORTED_SYMBOLS = (
+    "sm100_fp8_grouped_wgrad",
+    "sm100_wgrad_quantize_1x128",
+    "sm100_wgrad_build_meta",
+    "sm100_wgrad_device_error",
+    "sm100_wgrad_status_string",
+    "sm100_wgrad_version",
+)
+
+
+class Sm100WgradArgs(ctypes.Structure):
+    _fields_ = [
+        ("lhs_data", ctypes.c_void_p),
+        ("lhs_pitch", ctypes.c_int64),
+        ("lhs_scales", ctypes.c_void_p),
+        ("rhs_data", ctypes.c_void_p),
+        ("rhs_pitch", ctypes.c_int64),
+        ("rhs_scales", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("out_dtype", ctypes.c_int32),
+        ("accumulate", ctypes.c_int32),
+        ("num_experts", ctypes.c_int64),
+        ("m", ctypes.c_int64),
+        ("n", ctypes.c_int64),
+        ("k_rows", ctypes.c_int64),
+        ("total_blocks", ctypes.c_int64),
+        ("block_offsets", ctypes.c_void_p),
+        ("k_row_offsets", ctypes.c_void_p),
+        ("expert_order", ctypes.c_void_p),
+        ("tile_config", ctypes.c_int32),
+        ("max_ctas", ctypes.c_int32),
+    ]
+
+
+class Sm100WgradMetaOut(ctypes.Structure):
+    _fields_ = [
+        ("blocks_per_expert", ctypes.c_void_p),
+        ("block_offsets", ctypes.c_void_p),
+        ("padded_cu_seqlens_k", ctypes.c_void_p),
+        ("wgmma_cu_seqlens_k", ctypes.c_void_p),
+        ("tail_valid_rows", ctypes.c_void_p),
+        ("tail_wgmma_atoms", ctypes.c_void_p),
+        ("tail_copy_k", ctypes.c_void_p),
+        ("has_tail", ctypes.c_void_p),
+        ("expert_order", ctypes.c_void_p),
+        ("block_row_start", ctypes.c_void_p),
+        ("block_row_count", ctypes.c_void_p),
+        ("wgmma_block_row_start", ctypes.c_void_p),
+        ("block_capacity", ctypes.c_int64),
+        ("totals", ctypes.c_void_p),
+    ]
+
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def library_path() -> Path:
+    override = os.environ.get("SM100_WGRAD_LIB")
+    return Path(override) if override else LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the C-ABI library; raise RuntimeError if absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = library_path()
+        if not path.is_file():
+            raise RuntimeError(
+                f"{LIB_NAME} not found at {path}; build it with "
+                "`python sm90-fp8-wgrad_b200/build_ext.py` (nvcc, sm_100a)"
+            )
+        try:
+            lib = ctypes.CDLL(str(path))
+        except OSError as exc:
+            raise RuntimeError(f"cannot load {path}: {exc}") from exc
+        lib.sm100_fp8_grouped_wgrad.argtypes = [ctypes.POINTER(Sm100WgradArgs), ctypes.c_void_p]
+        lib.sm100_fp8_grouped_wgrad.restype = ctypes.c_int
+        lib.sm100_wgrad_quantize_1x128.argtypes = [
+            ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+            ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+        ]
+        lib.sm100_wgrad_quantize_1x128.restype = ctypes.c_int
+        lib.sm100_wgrad_build_meta.argtypes = [
+            ctypes.c_void_p, ctypes.c_int64, ctypes.POINTER(Sm100WgradMetaOut), ctypes.c_void_p,
+        ]
+        lib.sm100_wgrad_build_meta.restype = ctypes.c_int
+        lib.sm100_wgrad_device_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
+        lib.sm100_wgrad_device_error.restype = ctypes.c_int
+        lib.sm100_wgrad_status_string.argtypes = [ctypes.c_int]
+        lib.sm100_wgrad_status_string.restype = ctypes.c_char_p
+        lib.sm100_wgrad_version.argtypes = []
+        lib.sm100_wgrad_version.restype = ctypes.c_char_p
+        _lib = lib
+        return lib
+
+
+def status_string(status: int) -> str:
+    return load().sm100_wgrad_status_string(int(status)).decode()
+
+
+def check(status: int, what: str) -> None:
+    """Map a non-zero C status to RuntimeError (the reference's error type)."""
+    if int(status) != OK:
+        raise RuntimeError(f"{what} failed: status {int(status)} ({status_string(status)})")
+
+
+def device_error() -> int:
+    """Read and clear the device error word of the current device (synchronous)."""
+    code = ctypes.c_int32(0)
+    check(load().sm100_wgrad_device_error(ctypes.byref(code)), "sm100_wgrad_device_error")
+    return int(code.value)
+
+
+def version() -> str:
+    return load().sm100_wgrad_version().decode()

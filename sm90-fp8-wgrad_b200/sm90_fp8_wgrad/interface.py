@@ -1,0 +1,209 @@
+"""Public grouped FP8 Wgrad operator (the drop-in boundary).
+
+``fp8_grouped_wgrad_sm90`` keeps the reference signature, validation messages
+and error type (src/sm90_fp8_wgrad/interface.py:28-69, 128-256); its body is a
+single call of the C-ABI entry point ``sm100_fp8_grouped_wgrad`` on the
+current CUDA stream. Unlike the reference implementation
+(gemm_sm90.py:5676) the call performs no device->host synchronisation, so
+back-to-back calls queue on the stream without host round trips.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Literal
+
+import torch
+
+from . import _lib
+from .block_meta import WgradScaleBlockMeta
+from .layout_mode import LAYOUT_MODE_PACKED, resolve_wgrad_layout_mode
+from .quant import Fp8GroupedWgradOperand
+
+# tuned_config names accepted by the reference (gemm_sm90.py:265-509), mapped
+# onto the B200 tile shapes. The SM90 cluster/pingpong variants have no
+# separate meaning on tcgen05: every name resolves to the persistent kernel
+# with a 128-row tile and the N width listed here (0 = choose by shape).
+TUNED_CONFIGS: dict[str, int] = {
+    "default": _lib.TILE_AUTO,
+    "optB_coop128_default": _lib.TILE_AUTO,
+    "down_128x192": _lib.TILE_128x256,
+    "down_128x128_pingpong": _lib.TILE_128x128,
+    "down_128x256": _lib.TILE_128x256,
+    "down_64x256": _lib.TILE_128x256,
+    "down_128x192_coop": _lib.TILE_128x256,
+    "down_128x256_coop": _lib.TILE_128x256,
+    "down_64x192": _lib.TILE_128x256,
+    "down_64x192_coop": _lib.TILE_128x256,
+    "gate_64x256": _lib.TILE_128x256,
+    "gate_64x192": _lib.TILE_128x256,
+    "gate_128x192": _lib.TILE_128x256,
+    "gate_128x256": _lib.TILE_128x256,
+    "gate_128x256_coop": _lib.TILE_128x256,
+    "gate_256x256_coop": _lib.TILE_128x256,
+    "gate_64x256_coop": _lib.TILE_128x256,
+    "gate_128x128": _lib.TILE_128x128,
+    "gate_256x128": _lib.TILE_128x128,
+    "optA_down_64x128_dbacc": _lib.TILE_128x128,
+    "optA_gate_64x128_dbacc": _lib.TILE_128x128,
+    "optB_down_64x128_wg_pingpong": _lib.TILE_128x128,
+    "optB_gate_64x128_wg_pingpong": _lib.TILE_128x128,
+    "tail64_64x128": _lib.TILE_128x128,
+    "tail64_64x256": _lib.TILE_128x256,
+    "tail32_64x128": _lib.TILE_128x128,
+    # B200-native names
+    "sm100_128x256": _lib.TILE_128x256,
+    "sm100_128x128": _lib.TILE_128x128,
+}
+
+
+def _check_fp8_operand(name: str, operand: Fp8GroupedWgradOperand) -> None:
+    """Operand checks of the reference (interface.py:28-69)."""
+    if operand.data.dtype != torch.float8_e4m3fn:
+        raise RuntimeError(f"{name}.data must be torch.float8_e4m3fn, got {operand.data.dtype}")
+    if operand.scales.dtype != torch.float32:
+        raise RuntimeError(f"{name}.scales must be torch.float32, got {operand.scales.dtype}")
+    if operand.data.ndim != 2 or operand.scales.ndim != 2:
+        raise RuntimeError(f"{name} must have data [K,N] and scales [B,N]")
+    if int(operand.data.shape[1]) != int(operand.scales.shape[1]):
+        raise RuntimeError(f"{name} data/scales column mismatch")
+    if int(operand.data.stride(0)) != 1:
+        raise RuntimeError(
+            f"{name}.data must be FP8 K-major logical [K,N] with stride(0) == 1, "
+            f"got stride={tuple(operand.data.stride())}"
+        )
+    if int(operand.data.stride(1)) % 16 != 0:
+        raise RuntimeError(
+            f"{name}.data leading dimension must be divisible by 16 for FP8 TMA, "
+            f"got stride={tuple(operand.data.stride())}"
+        )
+    if not operand.scales.is_contiguous():
+        raise RuntimeError(f"{name}.scales must be contiguous")
+
+
+def _auto_tuned_config(m: int, n: int) -> str:
+    """Shape-keyed config selection with the reference's env overrides
+    (interface.py:72-84)."""
+    fallback = os.environ.get("KERNEL_LAB_WGRAD_AUTO_FALLBACK", "default").strip() or "default"
+    if int(m) == 2048 and int(n) == 768:
+        return os.environ.get("KERNEL_LAB_WGRAD_AUTO_DOWN", fallback).strip() or fallback
+    if int(m) == 1536 and int(n) == 2048:
+        return os.environ.get("KERNEL_LAB_WGRAD_AUTO_GATE_UP", fallback).strip() or fallback
+    return fallback
+
+
+def _check_int_vector(name: str, t: torch.Tensor, length: int, device: torch.device) -> None:
+    if t.dtype != torch.int32:
+        raise RuntimeError(f"{name} must be int32")
+    if t.ndim != 1 or int(t.shape[0]) != length:
+        raise RuntimeError(f"{name} shape must be [{length}], got {tuple(t.shape)}")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    if t.device != device:
+        raise RuntimeError(f"{name} must be on {device}, got {t.device}")
+
+
+def fp8_grouped_wgrad_sm90(
+    lhs: Fp8GroupedWgradOperand,
+    rhs: Fp8GroupedWgradOperand,
+    out: torch.Tensor,
+    meta: WgradScaleBlockMeta,
+    *,
+    output_layout: Literal["emn"] = "emn",
+    tuned_config: str = "default",
+    accumulate: bool = False,
+) -> torch.Tensor:
+    """Grouped scaled FP8 Wgrad (runs the sm_100a engine; name kept for drop-in).
+
+    Contract (reference interface.py:138-155):
+      lhs.data   logical [K_rows, M], stride(0) == 1, stride(1) % 16 == 0
+      rhs.data   logical [K_rows, N], same layout
+      lhs.scales [total_blocks, M], rhs.scales [total_blocks, N]   fp32
+      out        [E, M, N] bf16 or fp32, contiguous
+
+      out[e, m, n] (+)= sum_b sum_{k in b} lhs_q[k,m] lhs_s[b,m] rhs_q[k,n] rhs_s[b,n]
+
+    with b over expert e's 128-row scale blocks; experts without rows give 0.
+    Runs on the current CUDA stream of ``out``'s device; returns ``out``.
+    """
+    layout_mode = resolve_wgrad_layout_mode()
+    _check_fp8_operand("lhs", lhs)
+    _check_fp8_operand("rhs", rhs)
+    if layout_mode == LAYOUT_MODE_PACKED:
+        raise RuntimeError("packed layout is not implemented by the B200 engine yet; use padded")
+    expected_k_rows = int(meta.padded_rows)
+    if lhs.data.shape[0] != rhs.data.shape[0]:
+        raise RuntimeError(
+            "lhs/rhs K_rows mismatch: "
+            f"lhs={tuple(lhs.data.shape)} stride={tuple(lhs.data.stride())} "
+            f"rhs={tuple(rhs.data.shape)} stride={tuple(rhs.data.stride())} "
+            f"layout_mode={layout_mode!r}"
+        )
+    if int(lhs.data.shape[0]) != expected_k_rows:
+        raise RuntimeError(
+            f"operand K_rows does not match metadata for layout_mode={layout_mode!r}: "
+            f"got {int(lhs.data.shape[0])}, expected {expected_k_rows}"
+        )
+    if lhs.scales.shape[0] != rhs.scales.shape[0]:
+        raise RuntimeError("lhs/rhs scale block count mismatch")
+    if int(lhs.scales.shape[0]) != int(meta.total_blocks):
+        raise RuntimeError("scale block count does not match metadata")
+    if out.ndim != 3:
+        raise RuntimeError(f"expected out [E,M,N], got {tuple(out.shape)}")
+    if out.dtype not in (torch.bfloat16, torch.float32):
+        raise RuntimeError(f"out dtype must be bf16 or fp32, got {out.dtype}")
+    if output_layout != "emn":
+        raise RuntimeError("only contiguous [E,M,N] output is implemented for the benchmark")
+    if not out.is_contiguous():
+        raise RuntimeError("custom FP8 Wgrad output must be contiguous [E,M,N]")
+    if not out.is_cuda:
+        raise RuntimeError("out must be a CUDA tensor")
+    experts, m, n = map(int, out.shape)
+    if int(lhs.data.shape[1]) != m or int(rhs.data.shape[1]) != n:
+        raise RuntimeError(
+            f"out [E,M,N]={tuple(out.shape)} does not match lhs cols {int(lhs.data.shape[1])} "
+            f"and rhs cols {int(rhs.data.shape[1])}"
+        )
+    dev = out.device
+    for name, t in (("lhs.data", lhs.data), ("rhs.data", rhs.data), ("lhs.scales", lhs.scales),
+                    ("rhs.scales", rhs.scales)):
+        if t.device != dev:
+            raise RuntimeError(f"{name} must be on {dev}, got {t.device}")
+    _check_int_vector("cu_seqlens_k", meta.padded_cu_seqlens_k, experts + 1, dev)
+    _check_int_vector("block_offsets", meta.block_offsets, experts + 1, dev)
+    order = meta.expert_order
+    if order is not None:
+        _check_int_vector("expert_order", order, experts, dev)
+    resolved = _auto_tuned_config(m, n) if tuned_config == "auto" else str(tuned_config)
+    if resolved not in TUNED_CONFIGS:
+        raise RuntimeError(f"unknown Wgrad config {resolved!r}; choices={sorted(TUNED_CONFIGS)}")
+
+    args = _lib.Sm100WgradArgs()
+    args.lhs_data = lhs.data.data_ptr()
+    args.lhs_pitch = int(lhs.data.stride(1))
+    args.lhs_scales = lhs.scales.data_ptr()
+    args.rhs_data = rhs.data.data_ptr()
+    args.rhs_pitch = int(rhs.data.stride(1))
+    args.rhs_scales = rhs.scales.data_ptr()
+    args.out = out.data_ptr()
+    args.out_dtype = _lib.OUT_BF16 if out.dtype == torch.bfloat16 else _lib.OUT_F32
+    args.accumulate = 1 if accumulate else 0
+    args.num_experts = experts
+    args.m = m
+    args.n = n
+    args.k_rows = expected_k_rows
+    args.total_blocks = int(meta.total_blocks)
+    args.block_offsets = meta.block_offsets.data_ptr()
+    args.k_row_offsets = meta.padded_cu_seqlens_k.data_ptr()
+    args.expert_order = order.data_ptr() if order is not None and experts > 0 else None
+    args.tile_config = TUNED_CONFIGS[resolved]
+    args.max_ctas = int(os.environ.get("SM100_WGRAD_MAX_CTAS", "0") or 0)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        status = lib.sm100_fp8_grouped_wgrad(ctypes.byref(args), torch.cuda.current_stream().cuda_stream)
+    _lib.check(status, "sm100_fp8_grouped_wgrad")
+    return out
+
+
+# B200-native alias of the same operator.
+fp8_grouped_wgrad_sm100 = fp8_grouped_wgrad_sm90

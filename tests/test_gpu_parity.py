@@ -1,0 +1,216 @@
+"""GPU parity: the CUDA metadata builder, quantiser and grouped Wgrad GEMM
+(all through the C-ABI library) against the CPU oracle.
+
+Tolerances (FP8 operands are identical bytes on both sides, so only the
+accumulation order and the final rounding differ):
+  * metadata, FP8 bytes and scales: bit-exact;
+  * BF16 output vs the oracle's fp32 result: DeepSeek calc_diff <= 1e-5 (the
+    contract gate), calc_diff vs the BF16-rounded oracle <= 1e-6, and
+    elementwise |gpu - ref| <= 2^-7 |ref| + 1e-5 max|ref| (one BF16 ulp plus
+    fp32 accumulation-order noise);
+  * fp32 output: calc_diff <= 1e-9, |gpu - ref| <= 1e-4 |ref| + 1e-6 max|ref|.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import wgrad_oracle as O
+from golden_inputs import C1, SMALL_CASES, case_inputs
+
+pytestmark = pytest.mark.gpu
+
+STAGES = {"down": ("lhs_down", "rhs_down"), "gate": ("lhs_gate", "rhs_gate")}
+
+
+def _cu(counts):
+    return np.concatenate([[0], np.cumsum(np.asarray(counts, np.int64))]).astype(np.int64)
+
+
+def _gpu_case(spec, dev, x_dtype=torch.bfloat16):
+    from sm90_fp8_wgrad import build_wgrad_scale_block_meta, quantize_grouped_wgrad_operand_128x1
+
+    cu = torch.from_numpy(_cu(spec["counts"])).to(device=dev, dtype=torch.int32)
+    meta = build_wgrad_scale_block_meta(cu)
+    inp = case_inputs(spec)
+    ops = {k: quantize_grouped_wgrad_operand_128x1(torch.from_numpy(v).to(dev).to(x_dtype), meta)
+           for k, v in inp.items()}
+    return meta, inp, ops
+
+
+def _oracle_case(spec):
+    meta = O.build_meta(_cu(spec["counts"]))
+    inp = case_inputs(spec)
+    return meta, {k: O.quantize_1x128(v, meta) for k, v in inp.items()}
+
+
+def _check_bf16(out_gpu: torch.Tensor, ref: np.ndarray):
+    got = out_gpu.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    if ref.size == 0 or not np.abs(ref).max() > 0:
+        np.testing.assert_array_equal(got, 0.0)
+        return {"calc_diff": 0.0}
+    cd = O.calc_diff(got, ref)
+    cd_b = O.calc_diff(got, O.bf16_round(ref))
+    assert cd <= 1e-5, cd
+    assert cd_b <= 1e-6, cd_b
+    scale = float(np.abs(ref).max())
+    np.testing.assert_allclose(got, ref, rtol=2 ** -7, atol=1e-5 * scale)
+    return {"calc_diff": cd, "calc_diff_bf16": cd_b, "max_rel": O.scaled_wgrad_error(got, ref)[1]}
+
+
+def _check_f32(out_gpu: torch.Tensor, ref: np.ndarray):
+    got = out_gpu.cpu().numpy()
+    assert np.isfinite(got).all()
+    if not np.abs(ref).max() > 0:
+        np.testing.assert_array_equal(got, 0.0)
+        return
+    assert O.calc_diff(got, ref) <= 1e-9
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-6 * float(np.abs(ref).max()))
+
+
+@pytest.mark.parametrize("case", sorted(SMALL_CASES) + ["c1"])
+def test_meta_builder_matches_oracle(cuda_device, case):
+    from sm90_fp8_wgrad import build_wgrad_scale_block_meta
+
+    spec = C1 if case == "c1" else SMALL_CASES[case]
+    om = O.build_meta(_cu(spec["counts"]))
+    gm = build_wgrad_scale_block_meta(torch.from_numpy(_cu(spec["counts"])).to(cuda_device, torch.int32))
+    for f in ("padded_cu_seqlens_k", "wgmma_cu_seqlens_k", "tma_cu_seqlens_k", "blocks_per_expert",
+              "block_offsets", "block_row_start", "wgmma_block_row_start", "tma_block_row_start",
+              "block_row_count", "tail_valid_rows", "tail_wgmma_atoms", "tail_copy_k", "has_tail"):
+        np.testing.assert_array_equal(getattr(gm, f).cpu().numpy().astype(np.int64),
+                                      np.asarray(getattr(om, f)).astype(np.int64), err_msg=f)
+    for f in ("valid_rows", "padded_rows", "wgmma_rows", "tma_rows", "total_blocks"):
+        assert getattr(gm, f) == getattr(om, f), f
+    np.testing.assert_array_equal(gm.expert_order.cpu().numpy(), O.lpt_expert_order(om.blocks_per_expert))
+
+
+@pytest.mark.parametrize("counts", [[0, 0, 0, 0], [1, 31, 32, 33, 63, 64, 65, 127, 128, 129, 255, 256, 257],
+                                    [70000, 0, 17, 4096], list(range(0, 3000, 7))])
+def test_meta_builder_edge_routings(cuda_device, counts):
+    from sm90_fp8_wgrad import build_wgrad_scale_block_meta
+
+    om = O.build_meta(_cu(counts))
+    gm = build_wgrad_scale_block_meta(torch.from_numpy(_cu(counts)).to(cuda_device, torch.int32))
+    for f in ("block_offsets", "block_row_start", "block_row_count", "wgmma_cu_seqlens_k", "wgmma_block_row_start"):
+        np.testing.assert_array_equal(getattr(gm, f).cpu().numpy().astype(np.int64), getattr(om, f), err_msg=f)
+    assert gm.total_blocks == om.total_blocks
+
+
+def test_meta_builder_rejects_non_monotonic(cuda_device):
+    from sm90_fp8_wgrad import build_wgrad_scale_block_meta
+
+    with pytest.raises(RuntimeError, match="monotonic"):
+        build_wgrad_scale_block_meta(torch.tensor([0, 10, 5], dtype=torch.int32, device=cuda_device))
+
+
+@pytest.mark.parametrize("case", sorted(SMALL_CASES) + ["c1"])
+def test_quantiser_bit_exact(cuda_device, case):
+    spec = C1 if case == "c1" else SMALL_CASES[case]
+    meta, inp, ops = _gpu_case(spec, cuda_device)
+    om, oops = _oracle_case(spec)
+    for k, op in ops.items():
+        pitch = op.data.stride(1)
+        storage = op.data.as_strided((op.data.shape[1], pitch), (pitch, 1)).view(torch.uint8).cpu().numpy()
+        np.testing.assert_array_equal(storage[:, : om.padded_rows], oops[k].data[:, : om.padded_rows], err_msg=k)
+        np.testing.assert_array_equal(op.scales.cpu().numpy().view(np.uint32), oops[k].scales.view(np.uint32),
+                                      err_msg=k)
+
+
+def test_quantiser_fp32_input_and_odd_columns(cuda_device):
+    """fp32 source, a column count that is not a multiple of the 64-column tile."""
+    from sm90_fp8_wgrad import build_wgrad_scale_block_meta, quantize_grouped_wgrad_operand_128x1
+
+    counts = [5, 200, 0, 129]
+    rng = np.random.Generator(np.random.PCG64(3))
+    x = (rng.standard_normal((sum(counts), 72), dtype=np.float32) * np.float32(3.0))
+    x[7, 3] = 0.0
+    x[:, 5] = 0.0                                  # all-zero column -> scale floor 1e-12
+    om = O.build_meta(_cu(counts))
+    ref = O.quantize_1x128(x, om)
+    meta = build_wgrad_scale_block_meta(torch.from_numpy(_cu(counts)).to(cuda_device, torch.int32))
+    op = quantize_grouped_wgrad_operand_128x1(torch.from_numpy(x).to(cuda_device), meta)
+    pitch = op.data.stride(1)
+    storage = op.data.as_strided((72, pitch), (pitch, 1)).view(torch.uint8).cpu().numpy()
+    np.testing.assert_array_equal(storage[:, : om.padded_rows], ref.data[:, : om.padded_rows])
+    np.testing.assert_array_equal(op.scales.cpu().numpy().view(np.uint32), ref.scales.view(np.uint32))
+
+
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x128", "sm100_128x256"])
+@pytest.mark.parametrize("case", sorted(SMALL_CASES) + ["c1"])
+def test_grouped_wgrad_matches_oracle(cuda_device, case, tuned_config):
+    from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
+
+    spec = C1 if case == "c1" else SMALL_CASES[case]
+    meta, _, ops = _gpu_case(spec, cuda_device)
+    om, oops = _oracle_case(spec)
+    e = len(spec["counts"])
+    for stage, (lk, rk) in STAGES.items():
+        m, n = ops[lk].data.shape[1], ops[rk].data.shape[1]
+        out = torch.full((e, m, n), float("nan"), device=cuda_device, dtype=torch.bfloat16)  # poison
+        fp8_grouped_wgrad_sm90(ops[lk], ops[rk], out, meta, tuned_config=tuned_config)
+        torch.cuda.synchronize()
+        ref = O.ref_scaled_wgrad(oops[lk], oops[rk], om)
+        _check_bf16(out, ref)
+    from sm90_fp8_wgrad import _lib
+
+    assert _lib.device_error() == 0
+
+
+def test_grouped_wgrad_fp32_out_and_accumulate(cuda_device):
+    from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
+
+    spec = SMALL_CASES["mixed"]
+    meta, _, ops = _gpu_case(spec, cuda_device)
+    om, oops = _oracle_case(spec)
+    e = len(spec["counts"])
+    lk, rk = STAGES["gate"]
+    m, n = ops[lk].data.shape[1], ops[rk].data.shape[1]
+    ref = O.ref_scaled_wgrad(oops[lk], oops[rk], om)
+    out = torch.full((e, m, n), float("nan"), device=cuda_device, dtype=torch.float32)
+    fp8_grouped_wgrad_sm90(ops[lk], ops[rk], out, meta)
+    _check_f32(out, ref)
+    base = torch.randn((e, m, n), device=cuda_device, dtype=torch.float32) * float(np.abs(ref).max())
+    acc = base.clone()
+    fp8_grouped_wgrad_sm90(ops[lk], ops[rk], acc, meta, accumulate=True)
+    _check_f32(acc - base, ref)
+    base16 = base.to(torch.bfloat16)
+    acc16 = base16.clone()
+    fp8_grouped_wgrad_sm90(ops[lk], ops[rk], acc16, meta, accumulate=True)
+    expect = O.bf16_round(base16.float().cpu().numpy() + ref)
+    got = acc16.float().cpu().numpy()
+    np.testing.assert_allclose(got, expect, rtol=2 ** -7, atol=1e-5 * float(np.abs(expect).max()))
+
+
+@pytest.mark.parametrize("hidden,inter", [(144, 80), (272, 48), (512, 128)])
+def test_grouped_wgrad_ragged_tiles(cuda_device, hidden, inter):
+    """M, N not multiples of the 128 x 256 tile; empty experts; long K."""
+    from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
+
+    spec = {"counts": [0, 640, 3, 129, 0, 1100], "tokens": 700, "hidden": hidden, "intermediate": inter, "seed": 5}
+    meta, _, ops = _gpu_case(spec, cuda_device)
+    om, oops = _oracle_case(spec)
+    for stage, (lk, rk) in STAGES.items():
+        m, n = ops[lk].data.shape[1], ops[rk].data.shape[1]
+        out = torch.full((6, m, n), float("nan"), device=cuda_device, dtype=torch.bfloat16)
+        fp8_grouped_wgrad_sm90(ops[lk], ops[rk], out, meta)
+        _check_bf16(out, O.ref_scaled_wgrad(oops[lk], oops[rk], om))
+
+
+def test_interface_validation_errors(cuda_device):
+    from sm90_fp8_wgrad import Fp8GroupedWgradOperand, fp8_grouped_wgrad_sm90
+
+    spec = SMALL_CASES["single"]
+    meta, _, ops = _gpu_case(spec, cuda_device)
+    lhs, rhs = ops["lhs_down"], ops["rhs_down"]
+    out = torch.empty((1, lhs.data.shape[1], rhs.data.shape[1]), device=cuda_device, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="float8_e4m3fn"):
+        fp8_grouped_wgrad_sm90(Fp8GroupedWgradOperand(lhs.data.view(torch.uint8), lhs.scales), rhs, out, meta)
+    with pytest.raises(RuntimeError, match="out dtype"):
+        fp8_grouped_wgrad_sm90(lhs, rhs, out.half(), meta)
+    with pytest.raises(RuntimeError, match="unknown Wgrad config"):
+        fp8_grouped_wgrad_sm90(lhs, rhs, out, meta, tuned_config="nope")
+    with pytest.raises(RuntimeError, match="contiguous"):
+        fp8_grouped_wgrad_sm90(lhs, rhs, out.transpose(1, 2), meta)

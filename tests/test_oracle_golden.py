@@ -1,0 +1,139 @@
+"""Pin the CPU oracle to the reference's own outputs (golden fixtures)."""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+import wgrad_oracle as O
+from golden_inputs import C1, META_CASES, SMALL_CASES, case_inputs
+
+MODES = ("masked128", "adaptive64", "adaptive32_64_128", "adaptive32_64_twophase")
+META_FIELDS = ("cu_seqlens_k", "padded_cu_seqlens_k", "wgmma_cu_seqlens_k", "tma_cu_seqlens_k",
+               "blocks_per_expert", "block_offsets", "block_row_start", "wgmma_block_row_start",
+               "tma_block_row_start", "block_row_count", "tail_valid_rows", "tail_wgmma_atoms",
+               "tail_copy_k", "has_tail")
+META_SCALARS = ("valid_rows", "padded_rows", "wgmma_rows", "tma_rows", "total_blocks")
+
+
+@pytest.fixture(scope="module")
+def meta_npz(golden_dir):
+    return np.load(golden_dir / "meta_cases.npz")
+
+
+def _cu(counts):
+    return np.concatenate([[0], np.cumsum(np.asarray(counts, np.int64))]).astype(np.int64)
+
+
+@pytest.mark.parametrize("case", sorted(META_CASES))
+@pytest.mark.parametrize("mode", MODES)
+def test_oracle_meta_matches_reference(meta_npz, case, mode):
+    m = O.build_meta(_cu(META_CASES[case]), packed_tail_tma_mode=mode)
+    for f in META_FIELDS:
+        np.testing.assert_array_equal(np.asarray(getattr(m, f)).astype(np.int64), meta_npz[f"{case}.{mode}.{f}"],
+                                      err_msg=f"{case}/{mode}/{f}")
+    for f in META_SCALARS:
+        assert int(getattr(m, f)) == int(meta_npz[f"{case}.{mode}.{f}"]), (case, mode, f)
+
+
+@pytest.mark.parametrize("case", sorted(META_CASES))
+def test_host_tail_and_full_split_builders_match_reference(meta_npz, case):
+    """The package's tensor-logic builders (run here on CPU tensors)."""
+    from sm90_fp8_wgrad import block_meta as BM
+
+    cu = torch.from_numpy(_cu(META_CASES[case])).to(torch.int32)
+    for tbk in (32, 64):
+        t = BM.build_wgrad_tail_block_meta(cu, tail_block_k=tbk, _require_cuda=False)
+        for f in META_FIELDS:
+            np.testing.assert_array_equal(getattr(t.meta, f).numpy().astype(np.int64),
+                                          meta_npz[f"{case}.tail{tbk}.{f}"], err_msg=f"tail{tbk}/{f}")
+        for f in META_SCALARS:
+            assert int(getattr(t.meta, f)) == int(meta_npz[f"{case}.tail{tbk}.{f}"]), f
+        np.testing.assert_array_equal(t.tail_indices.numpy(), meta_npz[f"{case}.tail{tbk}.tail_indices"])
+    s = BM.build_wgrad_full_block_split(cu, _require_cuda=False)
+    for f in META_FIELDS:
+        np.testing.assert_array_equal(getattr(s.full_meta, f).numpy().astype(np.int64),
+                                      meta_npz[f"{case}.full.{f}"], err_msg=f"full/{f}")
+    np.testing.assert_array_equal(s.tail_indices.numpy(), meta_npz[f"{case}.full.tail_indices"])
+    np.testing.assert_array_equal(s.tail_cu_seqlens_k.numpy(), meta_npz[f"{case}.full.tail_cu_seqlens_k"])
+    assert s.full_rows == int(meta_npz[f"{case}.full.full_rows"])
+    assert s.tail_rows == int(meta_npz[f"{case}.full.tail_rows"])
+
+
+def test_e4m3_encode_matches_torch_cast_exhaustively():
+    """Every e4m3 value, every midpoint between neighbours (ties) and nearby
+    values, compared with PyTorch's round-to-nearest-even cast."""
+    codes = np.arange(0, 0x7F, dtype=np.uint8)            # finite non-negative codes
+    vals = O.e4m3_decode(codes).astype(np.float64)
+    mids = (vals[:-1] + vals[1:]) / 2
+    probes = np.concatenate([vals, mids, np.nextafter(mids.astype(np.float32), np.float32(0)),
+                             np.nextafter(mids.astype(np.float32), np.float32(1e9)),
+                             np.linspace(0, 448, 20001), np.geomspace(1e-6, 448, 20001),
+                             [2.0 ** -10, 2.0 ** -9 * 0.5, 447.9, 448.0, 448.0001]]).astype(np.float32)
+    probes = np.concatenate([probes, -probes])
+    ours = O.e4m3_encode(probes)
+    ref = torch.from_numpy(probes).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    np.testing.assert_array_equal(ours, ref)
+    # saturation above the finite range (the CUDA conversion is satfinite)
+    assert O.e4m3_encode(np.float32(1000.0)) == 0x7E
+    assert O.e4m3_encode(np.float32(-1000.0)) == 0xFE
+
+
+@pytest.mark.parametrize("case", sorted(SMALL_CASES))
+def test_oracle_quantiser_matches_reference(golden_dir, case):
+    q = np.load(golden_dir / "quant_small.npz")
+    spec = SMALL_CASES[case]
+    meta = O.build_meta(_cu(spec["counts"]))
+    inp = case_inputs(spec)
+    for key in ("lhs_down", "rhs_down", "lhs_gate", "rhs_gate"):
+        op = O.quantize_1x128(inp[key], meta)
+        np.testing.assert_array_equal(op.data, q[f"{case}.{key}.data"], err_msg=key)
+        np.testing.assert_array_equal(op.scales.view(np.uint32), q[f"{case}.{key}.scales"].view(np.uint32),
+                                      err_msg=key)
+
+
+@pytest.mark.parametrize("case", sorted(SMALL_CASES))
+def test_oracle_wgrad_matches_reference(golden_dir, case):
+    w = np.load(golden_dir / "wgrad_small.npz")
+    spec = SMALL_CASES[case]
+    meta = O.build_meta(_cu(spec["counts"]))
+    inp = case_inputs(spec)
+    for stage, (lk, rk) in {"down": ("lhs_down", "rhs_down"), "gate": ("lhs_gate", "rhs_gate")}.items():
+        out = O.ref_scaled_wgrad(O.quantize_1x128(inp[lk], meta), O.quantize_1x128(inp[rk], meta), meta)
+        ref = w[f"{case}.{stage}.ref_f32"]
+        assert out.shape == ref.shape
+        # fp32 sums in a different order than the reference's torch matmul
+        np.testing.assert_allclose(out, ref, rtol=2e-5, atol=1e-6 * max(1.0, float(np.abs(ref).max())))
+        assert O.calc_diff(out, ref) <= 1e-10
+        # calc_diff / error summary restatements vs the reference's numbers. The
+        # reference sums in fp32, so its 1 - 2 sum(xy)/sum(x^2+y^2) carries an
+        # absolute error of order 1e-7 (sums of ~1e3 terms, ratio 1 - O(1e-6));
+        # the oracle sums in float64, hence atol 3e-7.
+        ref_bf16 = O.bf16_bits_to_f32(w[f"{case}.{stage}.ref_bf16"])
+        np.testing.assert_allclose(O.calc_diff(ref_bf16, ref), float(w[f"{case}.{stage}.calc_diff_bf16_vs_f32"]),
+                                   rtol=0, atol=3e-7)
+        np.testing.assert_allclose(O.scaled_wgrad_error(ref_bf16, ref),
+                                   w[f"{case}.{stage}.error_bf16_vs_f32"], rtol=1e-6)
+
+
+def test_oracle_c1_tiny_matches_reference(golden_dir):
+    g = np.load(golden_dir / "c1_tiny.npz")
+    np.testing.assert_array_equal(np.asarray(C1["counts"]), g["counts"])
+    meta = O.build_meta(_cu(C1["counts"]))
+    inp = case_inputs(C1)
+    ops = {}
+    for key in ("lhs_down", "rhs_down", "lhs_gate", "rhs_gate"):
+        op = O.quantize_1x128(inp[key], meta)
+        assert hashlib.sha256(op.data.tobytes()).hexdigest() == str(g[f"{key}.data_sha256"]), key
+        assert hashlib.sha256(op.scales.tobytes()).hexdigest() == str(g[f"{key}.scales_sha256"]), key
+        ops[key] = op
+    for stage, (lk, rk) in {"down": ("lhs_down", "rhs_down"), "gate": ("lhs_gate", "rhs_gate")}.items():
+        out = O.ref_scaled_wgrad(ops[lk], ops[rk], meta)
+        np.testing.assert_allclose(out.reshape(out.shape[0], -1).sum(1, dtype=np.float64), g[f"{stage}.expert_sum"],
+                                   rtol=1e-4, atol=1e-6)
+        np.testing.assert_allclose((out.astype(np.float64) ** 2).reshape(out.shape[0], -1).sum(1),
+                                   g[f"{stage}.expert_sumsq"], rtol=1e-5)
+        np.testing.assert_allclose(out.reshape(-1)[g[f"{stage}.sample_idx"]], g[f"{stage}.sample"],
+                                   rtol=1e-4, atol=1e-7)
