@@ -350,6 +350,7 @@ def run_ours(args) -> None:
                 "peak": float(peaks["hbm_gbs"]), "unit": "GB/s", "frac": gbs / float(peaks["hbm_gbs"]),
                 "peak_source": "measured copy bandwidth (MEASURED_PEAKS.json)"}
     roof["traffic"] = _profile_traffic(args.workload)
+    roof["traffic_unit"] = "DRAM bytes per gate_up launch (ncu, profiles/grouped_wgrad_kernel_dsv3_32k_launches.md)"
     roof["step_roofline_ms"] = max(t_tc, t_hbm) * 1e3
     roof["step_roofline_frac"] = max(t_tc, t_hbm) * 1e3 / local_ms
 
