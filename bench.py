@@ -349,8 +349,11 @@ def run_ours(args) -> None:
         roof = {"bound": "hbm", "kernel": "grouped_wgrad_kernel<256> (gate_up launch)", "achieved": gbs,
                 "peak": float(peaks["hbm_gbs"]), "unit": "GB/s", "frac": gbs / float(peaks["hbm_gbs"]),
                 "peak_source": "measured copy bandwidth (MEASURED_PEAKS.json)"}
-    roof["traffic"] = _profile_traffic(args.workload)
-    roof["traffic_unit"] = "DRAM bytes per gate_up launch (ncu, profiles/grouped_wgrad_kernel_dsv3_32k_launches.md)"
+    traffic = _profile_traffic(args.workload)
+    # The ncu capture is of the 1-GPU launch; a rank's launch moves its experts' share.
+    roof["traffic"] = None if traffic is None else float(traffic) * (e1 - e0) / e_all
+    roof["traffic_unit"] = ("DRAM bytes per gate_up launch (ncu, profiles/grouped_wgrad_kernel_dsv3_32k_launches.md"
+                            + (", scaled by this rank's share of experts)" if world > 1 else ")"))
     roof["step_roofline_ms"] = max(t_tc, t_hbm) * 1e3
     roof["step_roofline_frac"] = max(t_tc, t_hbm) * 1e3 / local_ms
 

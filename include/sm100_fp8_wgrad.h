@@ -71,7 +71,7 @@ typedef struct Sm100WgradArgs {
   int64_t num_experts;       /* E                                                    */
   int64_t m;                 /* M (lhs columns)                                      */
   int64_t n;                 /* N (rhs columns)                                      */
-  int64_t k_rows;            /* operand K extent (padded rows)                       */
+  int64_t k_rows;            /* operand K extent (rows stored per column)            */
   int64_t total_blocks;      /* number of 128-row scale blocks                       */
   const int32_t* block_offsets;  /* device [E+1]                                     */
   const int32_t* k_row_offsets;  /* device [E+1]                                     */
@@ -86,6 +86,10 @@ typedef struct Sm100WgradArgs {
  * (the TVM-FFI launch of the CuTe-DSL kernel at gemm_sm90.py:5886), called from
  * fp8_grouped_wgrad_sm90, src/sm90_fp8_wgrad/interface.py:243-255.
  * Unlike the reference (gemm_sm90.py:5676) it performs no device->host read.
+ * Layouts: padded (k_row_offsets = 128 * block_offsets) or the reference's
+ * packed mode (k_row_offsets = wgmma_cu_seqlens_k, 32-row aligned expert
+ * starts, operands = kernel_data with >= 127 zero guard rows); an expert's last
+ * scale block multiplies only its ceil(rows / 32) valid 32-row K slices.
  */
 SM100_WGRAD_API int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* args, void* stream);
 
@@ -103,6 +107,44 @@ SM100_WGRAD_API int sm100_wgrad_quantize_1x128(const void* x, int32_t x_dtype, i
                                const int32_t* block_row_start, const int32_t* block_row_count,
                                int64_t total_blocks, void* q_data, int64_t q_pitch, float* scales,
                                void* stream);
+
+/*
+ * 1x128 FP8 quantiser, general form: the same math as sm100_wgrad_quantize_1x128
+ * with the destinations of the reference's two layout modes and an optional
+ * row gather.
+ *   x row of grouped row r : gather_idx ? gather_idx[r] : r     (token-major
+ *                            activation read through the MoE routing gather,
+ *                            fusing the gather of synthetic.py:132-150 into
+ *                            the quantiser; NULL = x is already grouped)
+ *   q_data                 : byte k of block b, column c at
+ *                            q[c * q_pitch + q_row_start[b] + k]
+ *                            (q_row_start NULL = 128 b: the padded layout);
+ *                            q_zero_fill != 0 also writes rows k >= count as 0
+ *   kq_data (optional)     : second copy at kq[c * kq_pitch + kq_row_start[b] + k],
+ *                            valid rows only (the caller zero-fills the buffer)
+ * Padded layout: quant.py:222-247; packed layout (data at block_row_start,
+ * kernel_data at wgmma_block_row_start): quant.py:196-266 and the Triton
+ * kernel's PACKED_LAYOUT / STORE_KERNEL_DATA branches, quant.py:129-167.
+ */
+typedef struct Sm100WgradQuantArgs {
+  const void* x;                  /* BF16 (x_dtype 0) or fp32 (1), row-major [x_rows][cols] */
+  int32_t x_dtype;
+  int64_t cols;
+  const int32_t* gather_idx;      /* [valid_rows] or NULL                                 */
+  const int32_t* block_row_start; /* [total_blocks] first grouped row of each block       */
+  const int32_t* block_row_count; /* [total_blocks] valid rows of each block              */
+  int64_t total_blocks;
+  void* q_data;
+  int64_t q_pitch;
+  const int32_t* q_row_start;     /* [total_blocks] or NULL                               */
+  int32_t q_zero_fill;
+  void* kq_data;                  /* or NULL                                              */
+  int64_t kq_pitch;
+  const int32_t* kq_row_start;    /* [total_blocks], required with kq_data                */
+  float* scales;                  /* [total_blocks][cols]                                 */
+} Sm100WgradQuantArgs;
+
+SM100_WGRAD_API int sm100_wgrad_quantize_1x128_ex(const Sm100WgradQuantArgs* args, void* stream);
 
 /*
  * Scale-block metadata builder (device side, no host sync).

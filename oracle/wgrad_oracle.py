@@ -15,6 +15,7 @@ It restates, in numpy, the reference's algorithm for every step of the path:
 * 1x128 FP8 quantiser       -- _quantize_grouped_wgrad_128x1_kernel,
                                src/sm90_fp8_wgrad/quant.py:129-167 and the
                                padded operand layout of quant.py:222-247
+* packed operand layout     -- quant.py:196-266 (data / kernel_data rows)
 * fp32 -> e4m3 conversion   -- round to nearest even, saturating to +-448
                                (written from the e4m3fn format definition:
                                1 sign, 4 exponent bits with bias 7, 3 mantissa
@@ -204,6 +205,36 @@ def quantize_1x128(x: np.ndarray, meta: OracleMeta) -> OracleOperand:
         q = (blk / scale[None, :]).astype(np.float32)                # x / scale, fp32
         data[:, b * BLOCK_K : b * BLOCK_K + n] = e4m3_encode(q).T
     return OracleOperand(data=data, scales=scales, k_rows=meta.padded_rows)
+
+
+_PACKED_GUARD_ROWS = {"masked128": 127, "adaptive64": 63, "adaptive32_64_128": 127, "adaptive32_64_twophase": 31}
+
+
+def packed_layout(op: OracleOperand, meta: OracleMeta, mode: str = "masked128") -> tuple[np.ndarray, np.ndarray]:
+    """Packed-layout storage of a quantised operand (same FP8 bytes, other rows).
+
+    quant.py:196-266 with the Triton kernel's PACKED_LAYOUT and STORE_KERNEL_DATA
+    branches (quant.py:133-167): ``data`` [cols, valid_rows] holds block b's valid
+    rows at block_row_start[b] + k; ``kernel_data`` [cols, base + guard] (zeros
+    elsewhere) holds them at the policy's block starts -- wgmma_block_row_start
+    for masked128, tma_block_row_start for the adaptive policies
+    (quant.py:47-95) -- with the guard rows of quant.py:66-83.
+    """
+    cols = op.data.shape[0]
+    data = np.zeros((cols, meta.valid_rows), dtype=np.uint8)
+    tma = mode != "masked128"
+    base = meta.tma_rows if tma else meta.wgmma_rows
+    starts = meta.tma_block_row_start if tma else meta.wgmma_block_row_start
+    guard = _PACKED_GUARD_ROWS[mode] if base > 0 else 0
+    kernel = np.zeros((cols, base + guard), dtype=np.uint8)
+    for b in range(meta.total_blocks):
+        n = int(meta.block_row_count[b])
+        src = op.data[:, b * BLOCK_K : b * BLOCK_K + n]
+        r0 = int(meta.block_row_start[b])
+        data[:, r0 : r0 + n] = src
+        k0 = int(starts[b])
+        kernel[:, k0 : k0 + n] = src
+    return data, kernel
 
 
 # ------------------------------------------------------- dequantised product

@@ -13,8 +13,10 @@
 #include "wgrad_gemm.cuh"
 
 namespace wgrad {
-cudaError_t launch_quantize_1x128(const void* x, int x_dtype, int64_t cols, const int32_t* block_row_start,
-                                  const int32_t* block_row_count, int64_t total_blocks, void* q, int64_t q_pitch,
+cudaError_t launch_quantize_1x128(const void* x, int x_dtype, int64_t cols, const int32_t* gather_idx,
+                                  const int32_t* block_row_start, const int32_t* block_row_count,
+                                  int64_t total_blocks, void* q, int64_t q_pitch, const int32_t* q_row_start,
+                                  bool q_zero_fill, void* kq, int64_t kq_pitch, const int32_t* kq_row_start,
                                   float* scales, cudaStream_t stream);
 cudaError_t launch_build_meta(const int32_t* cu, int64_t num_experts, const Sm100WgradMetaOut& out,
                               cudaStream_t stream);
@@ -154,7 +156,6 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
       return SM100_WGRAD_ERR_INVALID_ARG;
     if (a->lhs_pitch % 16 != 0 || a->rhs_pitch % 16 != 0 || a->lhs_pitch < a->k_rows || a->rhs_pitch < a->k_rows)
       return SM100_WGRAD_ERR_INVALID_ARG;
-    if (a->k_rows % 128 != 0) return SM100_WGRAD_ERR_UNSUPPORTED;  // padded layout: whole 128-row blocks
     if (!aligned16(a->lhs_data) || !aligned16(a->rhs_data) || !aligned16(a->lhs_scales) ||
         !aligned16(a->rhs_scales))
       return SM100_WGRAD_ERR_INVALID_ARG;
@@ -219,9 +220,31 @@ int sm100_wgrad_quantize_1x128(const void* x, int32_t x_dtype, int64_t valid_row
   DeviceInfo info;
   const int st = check_arch(&info);
   if (st != SM100_WGRAD_OK) return st;
-  const cudaError_t err = wgrad::launch_quantize_1x128(x, x_dtype, cols, block_row_start, block_row_count,
-                                                       total_blocks, q_data, q_pitch, scales,
-                                                       static_cast<cudaStream_t>(stream));
+  const cudaError_t err = wgrad::launch_quantize_1x128(x, x_dtype, cols, nullptr, block_row_start, block_row_count,
+                                                       total_blocks, q_data, q_pitch, nullptr, true, nullptr, 0,
+                                                       nullptr, scales, static_cast<cudaStream_t>(stream));
+  return err == cudaSuccess ? SM100_WGRAD_OK : SM100_WGRAD_ERR_LAUNCH;
+}
+
+int sm100_wgrad_quantize_1x128_ex(const Sm100WgradQuantArgs* a, void* stream) {
+  if (a == nullptr) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->x_dtype != 0 && a->x_dtype != 1) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->cols < 0 || a->total_blocks < 0 || a->q_pitch < 0 || a->kq_pitch < 0) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->total_blocks == 0 || a->cols == 0) return SM100_WGRAD_OK;
+  if (a->x == nullptr || a->block_row_start == nullptr || a->block_row_count == nullptr || a->q_data == nullptr ||
+      a->scales == nullptr)
+    return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->q_row_start == nullptr && (a->q_pitch < a->total_blocks * 128 || a->q_pitch % 16 != 0))
+    return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->kq_data != nullptr && a->kq_row_start == nullptr) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->total_blocks > INT32_MAX) return SM100_WGRAD_ERR_UNSUPPORTED;
+  DeviceInfo info;
+  const int st = check_arch(&info);
+  if (st != SM100_WGRAD_OK) return st;
+  const cudaError_t err = wgrad::launch_quantize_1x128(
+      a->x, a->x_dtype, a->cols, a->gather_idx, a->block_row_start, a->block_row_count, a->total_blocks, a->q_data,
+      a->q_pitch, a->q_row_start, a->q_zero_fill != 0, a->kq_data, a->kq_pitch, a->kq_row_start, a->scales,
+      static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? SM100_WGRAD_OK : SM100_WGRAD_ERR_LAUNCH;
 }
 

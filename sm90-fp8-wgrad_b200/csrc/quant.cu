@@ -11,6 +11,14 @@
 // conversion is round-to-nearest-even with saturation to the finite range, so
 // the bytes are reproducible on the CPU.
 //
+// Layouts: the padded operand (row b*128 + k, rows past the block's count
+// written as zeros), or the packed storage of the reference's packed layout
+// mode (quant.py:196-266: valid rows at block_row_start[b] + k in `data`, and a
+// second copy at wgmma_block_row_start[b] + k in the zero-initialised
+// `kernel_data`). An optional gather index reads the rows straight from a
+// token-major activation (row r of the grouped operand = x row gather_idx[r]),
+// which fuses the expert-major gather of the MoE backward into the quantiser.
+//
 // HBM-bound transpose: a CTA reads a 128-row x 64-column BF16 tile with
 // 16-byte coalesced loads, reduces column amax through shared memory and
 // writes each column's 128 FP8 bytes as one contiguous 128-byte segment
@@ -64,11 +72,22 @@ __device__ __forceinline__ float load1<float>(const float* src) {
 }
 
 // grid: (total_blocks, ceil(cols / 64)); block: 256 threads.
+// Destination of the quantised bytes: column c's byte k of block b goes to
+// q[c * pitch + row_start[b] + k] (row_start == nullptr: 128 b, the padded
+// layout). zero_fill also writes the zero rows k >= row_count of the block.
+struct QuantDst {
+  uint8_t* q;
+  int64_t pitch;
+  const int32_t* row_start;
+  bool zero_fill;
+};
+
 template <typename T>
 __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __restrict__ x, int64_t cols,
+                                                                  const int32_t* __restrict__ gather_idx,
                                                                   const int32_t* __restrict__ block_row_start,
                                                                   const int32_t* __restrict__ block_row_count,
-                                                                  uint8_t* __restrict__ q, int64_t q_pitch,
+                                                                  QuantDst d0, QuantDst d1,
                                                                   float* __restrict__ scales, bool vec_ok) {
   __shared__ float tile[QBLOCK_ROWS][QBLOCK_COLS + 1];
   __shared__ float s_amax[4][QBLOCK_COLS];
@@ -91,7 +110,8 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
       const int r = pass * 32 + r_in;
       float v[8];
       if (r < rows && cc < ncols) {
-        const T* src = x + (row0 + r) * cols + c0 + cc;
+        const int64_t xrow = gather_idx != nullptr ? static_cast<int64_t>(__ldg(gather_idx + row0 + r)) : row0 + r;
+        const T* src = x + xrow * cols + c0 + cc;
         if (vec_ok && cc + 8 <= ncols) {
           load8<T>(src, v);
         } else {
@@ -126,8 +146,8 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
   }
   __syncthreads();
 
-  // Store: column c's bytes q[c][128 b + k], k = 0..127, as 8 x 16-byte chunks.
-  const int64_t dst_row0 = static_cast<int64_t>(b) * QBLOCK_ROWS;
+  // Store: each 16-row chunk of column c's bytes as one 16-byte vector when the
+  // destination is aligned and the chunk is entirely written, else bytewise.
   for (int idx = tid; idx < QBLOCK_COLS * 8; idx += QTHREADS) {
     const int col = idx >> 3;
     const int chunk = idx & 7;
@@ -145,28 +165,44 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
       const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(f2, f3), __NV_SATFINITE, __NV_E4M3);
       w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
     }
-    uint8_t* dst = q + (c0 + col) * q_pitch + dst_row0 + chunk * 16;
-    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+#pragma unroll
+    for (int o = 0; o < 2; ++o) {
+      const QuantDst& d = o == 0 ? d0 : d1;
+      if (d.q == nullptr) continue;
+      const int64_t start = d.row_start != nullptr ? static_cast<int64_t>(__ldg(d.row_start + b))
+                                                   : static_cast<int64_t>(b) * QBLOCK_ROWS;
+      const int limit = d.zero_fill ? QBLOCK_ROWS : rows;  // rows k < limit are written
+      uint8_t* dst = d.q + (c0 + col) * d.pitch + start + chunk * 16;
+      if (chunk * 16 + 16 <= limit && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+      } else {
+        for (int i = 0; i < 16 && chunk * 16 + i < limit; ++i) dst[i] = static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3)));
+      }
+    }
   }
 }
 
 }  // namespace
 
-cudaError_t launch_quantize_1x128(const void* x, int x_dtype, int64_t cols, const int32_t* block_row_start,
-                                  const int32_t* block_row_count, int64_t total_blocks, void* q, int64_t q_pitch,
+cudaError_t launch_quantize_1x128(const void* x, int x_dtype, int64_t cols, const int32_t* gather_idx,
+                                  const int32_t* block_row_start, const int32_t* block_row_count,
+                                  int64_t total_blocks, void* q, int64_t q_pitch, const int32_t* q_row_start,
+                                  bool q_zero_fill, void* kq, int64_t kq_pitch, const int32_t* kq_row_start,
                                   float* scales, cudaStream_t stream) {
   if (total_blocks == 0 || cols == 0) return cudaSuccess;
   const dim3 grid(static_cast<unsigned>(total_blocks), static_cast<unsigned>((cols + QBLOCK_COLS - 1) / QBLOCK_COLS));
+  const QuantDst d0{static_cast<uint8_t*>(q), q_pitch, q_row_start, q_zero_fill};
+  const QuantDst d1{static_cast<uint8_t*>(kq), kq_pitch, kq_row_start, false};
   if (x_dtype == 0) {
     const bool vec_ok = (cols % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
     quantize_1x128_kernel<__nv_bfloat16><<<grid, QTHREADS, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(x), cols, block_row_start, block_row_count, static_cast<uint8_t*>(q),
-        q_pitch, scales, vec_ok);
+        static_cast<const __nv_bfloat16*>(x), cols, gather_idx, block_row_start, block_row_count, d0, d1, scales,
+        vec_ok);
   } else {
     const bool vec_ok = (cols % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
-    quantize_1x128_kernel<float><<<grid, QTHREADS, 0, stream>>>(static_cast<const float*>(x), cols, block_row_start,
-                                                               block_row_count, static_cast<uint8_t*>(q), q_pitch,
-                                                               scales, vec_ok);
+    quantize_1x128_kernel<float><<<grid, QTHREADS, 0, stream>>>(static_cast<const float*>(x), cols, gather_idx,
+                                                               block_row_start, block_row_count, d0, d1, scales,
+                                                               vec_ok);
   }
   return cudaGetLastError();
 }

@@ -193,7 +193,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       const TileCoord tc = decode_tile(p, tile);
       const int nkb = __ldg(p.block_offsets + tc.e + 1) - __ldg(p.block_offsets + tc.e);
+      // K slices of 32 rows in the expert's last block: 4 in the padded layout;
+      // in the packed layout only the slices that hold the expert's rows (the
+      // rest of the 128-row TMA box belongs to the next expert or the guard).
+      const int klen = __ldg(p.k_row_offsets + tc.e + 1) - __ldg(p.k_row_offsets + tc.e);
+      const int last_atoms = min(4, max(1, (klen - (nkb - 1) * BK + 31) / 32));
       for (int kb = 0; kb < nkb; ++kb) {
+        const int atoms = kb + 1 == nkb ? last_atoms : BK / 32;
         // Whole warp waits (keeps the warp converged for the .sync.aligned ops).
         ok = mbar_wait(&tempty_bar[acc], aphase ^ 1u, abort_flag, kDevTimeoutMma);
         if (ok) ok = mbar_wait(&full_bar[stage], phase, abort_flag, kDevTimeoutMma);
@@ -206,6 +212,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k) {
+            if (k >= atoms) break;
             // advance 32 bytes (one K=32 FP8 slice) inside the 128-byte swizzle atom
             umma_f8(d_tmem, umma_desc_k_sw128(a_addr + k * 32), umma_desc_k_sw128(b_addr + k * 32), idesc,
                     k > 0 ? 1u : 0u);

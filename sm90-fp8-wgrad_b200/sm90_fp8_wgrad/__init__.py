@@ -22,7 +22,12 @@ from .checks import (
     scaled_wgrad_stats,
 )
 from .interface import fp8_grouped_wgrad_sm90, fp8_grouped_wgrad_sm100
-from .quant import Fp8GroupedWgradOperand, quantize_grouped_wgrad_operand_128x1, quantize_grouped_wgrad_operand_tail_k
+from .quant import (
+    Fp8GroupedWgradOperand,
+    quantize_grouped_wgrad_operand_128x1,
+    quantize_grouped_wgrad_operand_128x1_gather,
+    quantize_grouped_wgrad_operand_tail_k,
+)
 
 __all__ = [
     "Fp8GroupedWgradOperand",
@@ -37,6 +42,7 @@ __all__ = [
     "fp8_grouped_wgrad_sm90",
     "fp8_grouped_wgrad_sm100",
     "quantize_grouped_wgrad_operand_128x1",
+    "quantize_grouped_wgrad_operand_128x1_gather",
     "quantize_grouped_wgrad_operand_tail_k",
     "ref_scaled_wgrad",
     "scaled_wgrad_error",

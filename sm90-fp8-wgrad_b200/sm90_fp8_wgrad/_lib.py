@@ -66,6 +66,28 @@ class Sm100WgradArgs(ctypes.Structure):
     ]
 
 
+class Sm100WgradQuantArgs(ctypes.Structure):
+    """Mirror of Sm100WgradQuantArgs (include/sm100_fp8_wgrad.h)."""
+
+    _fields_ = [
+        ("x", ctypes.c_void_p),
+        ("x_dtype", ctypes.c_int32),
+        ("cols", ctypes.c_int64),
+        ("gather_idx", ctypes.c_void_p),
+        ("block_row_start", ctypes.c_void_p),
+        ("block_row_count", ctypes.c_void_p),
+        ("total_blocks", ctypes.c_int64),
+        ("q_data", ctypes.c_void_p),
+        ("q_pitch", ctypes.c_int64),
+        ("q_row_start", ctypes.c_void_p),
+        ("q_zero_fill", ctypes.c_int32),
+        ("kq_data", ctypes.c_void_p),
+        ("kq_pitch", ctypes.c_int64),
+        ("kq_row_start", ctypes.c_void_p),
+        ("scales", ctypes.c_void_p),
+    ]
+
+
 class Sm100WgradMetaOut(ctypes.Structure):
     _fields_ = [
         ("blocks_per_expert", ctypes.c_void_p),
@@ -120,6 +142,8 @@ def load() -> ctypes.CDLL:
             ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
         ]
         lib.sm100_wgrad_quantize_1x128.restype = ctypes.c_int
+        lib.sm100_wgrad_quantize_1x128_ex.argtypes = [ctypes.POINTER(Sm100WgradQuantArgs), ctypes.c_void_p]
+        lib.sm100_wgrad_quantize_1x128_ex.restype = ctypes.c_int
         lib.sm100_wgrad_build_meta.argtypes = [
             ctypes.c_void_p, ctypes.c_int64, ctypes.POINTER(Sm100WgradMetaOut), ctypes.c_void_p,
         ]

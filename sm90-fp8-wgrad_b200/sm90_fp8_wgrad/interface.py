@@ -18,7 +18,12 @@ import torch
 from . import _lib
 from .block_meta import WgradScaleBlockMeta
 from .layout_mode import LAYOUT_MODE_PACKED, resolve_wgrad_layout_mode
-from .quant import Fp8GroupedWgradOperand
+from .quant import (
+    Fp8GroupedWgradOperand,
+    packed_kernel_data_base_rows,
+    packed_kernel_data_cu_seqlens_k,
+    packed_kernel_data_guard_rows,
+)
 
 # tuned_config names accepted by the reference (gemm_sm90.py:265-509), mapped
 # onto the B200 tile shapes. The SM90 cluster/pingpong variants have no
@@ -129,9 +134,8 @@ def fp8_grouped_wgrad_sm90(
     layout_mode = resolve_wgrad_layout_mode()
     _check_fp8_operand("lhs", lhs)
     _check_fp8_operand("rhs", rhs)
-    if layout_mode == LAYOUT_MODE_PACKED:
-        raise RuntimeError("packed layout is not implemented by the B200 engine yet; use padded")
-    expected_k_rows = int(meta.padded_rows)
+    packed = layout_mode == LAYOUT_MODE_PACKED
+    expected_k_rows = int(meta.valid_rows) if packed else int(meta.padded_rows)
     if lhs.data.shape[0] != rhs.data.shape[0]:
         raise RuntimeError(
             "lhs/rhs K_rows mismatch: "
@@ -144,6 +148,27 @@ def fp8_grouped_wgrad_sm90(
             f"operand K_rows does not match metadata for layout_mode={layout_mode!r}: "
             f"got {int(lhs.data.shape[0])}, expected {expected_k_rows}"
         )
+    if packed:
+        # reference interface.py:191-209: the launch copy must cover the packed
+        # K offsets plus the tail policy's TMA guard rows.
+        base_rows = packed_kernel_data_base_rows(meta)
+        for name, operand in (("lhs", lhs), ("rhs", rhs)):
+            kd = operand.kernel_data
+            if kd is None:
+                raise RuntimeError(f"packed {name}.kernel_data is required")
+            if int(kd.shape[1]) < base_rows:
+                raise RuntimeError(
+                    f"packed {name}.kernel_data K rows must cover meta.wgmma_rows: "
+                    f"got {tuple(kd.shape)}, expected at least K={base_rows}"
+                )
+            guard = packed_kernel_data_guard_rows(meta)
+            if base_rows > 0 and int(kd.shape[1]) < base_rows + guard:
+                raise RuntimeError(
+                    f"packed {name}.kernel_data must include a {guard}-row TMA guard: "
+                    f"got K={int(kd.shape[1])}, expected at least {base_rows + guard}"
+                )
+            if kd.dtype != torch.float8_e4m3fn or kd.ndim != 2 or int(kd.stride(1)) != 1 or int(kd.stride(0)) % 16:
+                raise RuntimeError(f"packed {name}.kernel_data must be float8_e4m3fn [cols, K] with K contiguous")
     if lhs.scales.shape[0] != rhs.scales.shape[0]:
         raise RuntimeError("lhs/rhs scale block count mismatch")
     if int(lhs.scales.shape[0]) != int(meta.total_blocks):
@@ -169,7 +194,8 @@ def fp8_grouped_wgrad_sm90(
                     ("rhs.scales", rhs.scales)):
         if t.device != dev:
             raise RuntimeError(f"{name} must be on {dev}, got {t.device}")
-    _check_int_vector("cu_seqlens_k", meta.padded_cu_seqlens_k, experts + 1, dev)
+    _check_int_vector("cu_seqlens_k", packed_kernel_data_cu_seqlens_k(meta) if packed else meta.padded_cu_seqlens_k,
+                      experts + 1, dev)
     _check_int_vector("block_offsets", meta.block_offsets, experts + 1, dev)
     order = meta.expert_order
     if order is not None:
@@ -179,11 +205,18 @@ def fp8_grouped_wgrad_sm90(
         raise RuntimeError(f"unknown Wgrad config {resolved!r}; choices={sorted(TUNED_CONFIGS)}")
 
     args = _lib.Sm100WgradArgs()
-    args.lhs_data = lhs.data.data_ptr()
-    args.lhs_pitch = int(lhs.data.stride(1))
+    if packed:
+        lk, rk = lhs.kernel_data, rhs.kernel_data
+        args.lhs_data, args.lhs_pitch = lk.data_ptr(), int(lk.stride(0))
+        args.rhs_data, args.rhs_pitch = rk.data_ptr(), int(rk.stride(0))
+        kernel_k_rows = min(int(lk.shape[1]), int(rk.shape[1]))
+        k_row_offsets = packed_kernel_data_cu_seqlens_k(meta)
+    else:
+        args.lhs_data, args.lhs_pitch = lhs.data.data_ptr(), int(lhs.data.stride(1))
+        args.rhs_data, args.rhs_pitch = rhs.data.data_ptr(), int(rhs.data.stride(1))
+        kernel_k_rows = expected_k_rows
+        k_row_offsets = meta.padded_cu_seqlens_k
     args.lhs_scales = lhs.scales.data_ptr()
-    args.rhs_data = rhs.data.data_ptr()
-    args.rhs_pitch = int(rhs.data.stride(1))
     args.rhs_scales = rhs.scales.data_ptr()
     args.out = out.data_ptr()
     args.out_dtype = _lib.OUT_BF16 if out.dtype == torch.bfloat16 else _lib.OUT_F32
@@ -191,10 +224,10 @@ def fp8_grouped_wgrad_sm90(
     args.num_experts = experts
     args.m = m
     args.n = n
-    args.k_rows = expected_k_rows
+    args.k_rows = kernel_k_rows
     args.total_blocks = int(meta.total_blocks)
     args.block_offsets = meta.block_offsets.data_ptr()
-    args.k_row_offsets = meta.padded_cu_seqlens_k.data_ptr()
+    args.k_row_offsets = k_row_offsets.data_ptr()
     args.expert_order = order.data_ptr() if order is not None and experts > 0 else None
     args.tile_config = TUNED_CONFIGS[resolved]
     args.max_ctas = int(os.environ.get("SM100_WGRAD_MAX_CTAS", "0") or 0)

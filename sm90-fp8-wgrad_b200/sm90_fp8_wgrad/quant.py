@@ -7,11 +7,14 @@ K contiguous, which is exactly the K-major operand layout tcgen05 reads --
 and ``scales`` is fp32 [total_blocks, cols].
 
 ``quantize_grouped_wgrad_operand_128x1`` runs the CUDA quantiser
-(``sm100_wgrad_quantize_1x128``), replacing the reference's Triton kernel
-(quant.py:105-167). It is input preparation, outside the timed region.
+(``sm100_wgrad_quantize_1x128_ex``), replacing the reference's Triton kernel
+(quant.py:105-167), for the padded and the packed layout;
+``quantize_grouped_wgrad_operand_128x1_gather`` fuses the expert-major row
+gather into it. Both are input preparation, outside the timed region.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -87,6 +90,68 @@ def operand_pitch(k_rows: int) -> int:
     return max(128, (int(k_rows) + 127) // 128 * 128)
 
 
+def _quantize(x: torch.Tensor, gather_idx: torch.Tensor | None, meta: WgradScaleBlockMeta,
+              layout_mode: str | None) -> Fp8GroupedWgradOperand:
+    """Shared body of the two quantiser entry points (one CUDA launch)."""
+    if x.ndim != 2:
+        raise RuntimeError(f"expected x_grouped [valid_TK,N], got {tuple(x.shape)}")
+    if not x.is_cuda:
+        raise RuntimeError("x_grouped must be CUDA")
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise RuntimeError(f"x_grouped must be bf16 or fp32, got {x.dtype}")
+    if not x.is_contiguous():
+        x = x.contiguous()
+    n = int(x.shape[1])
+    if gather_idx is None and int(meta.valid_rows) != int(x.shape[0]):
+        raise RuntimeError("meta.cu_seqlens_k[-1] must match x_grouped rows")
+    if int(meta.padded_rows) != int(meta.total_blocks) * int(meta.block_k):
+        raise RuntimeError("metadata padded_rows must equal total_blocks * block_k")
+    mode = resolve_wgrad_layout_mode(layout_mode)
+    dev = x.device
+    scales = torch.empty((int(meta.total_blocks), n), device=dev, dtype=torch.float32)
+    args = _lib.Sm100WgradQuantArgs()
+    args.x = x.data_ptr()
+    args.x_dtype = 0 if x.dtype == torch.bfloat16 else 1
+    args.cols = n
+    args.gather_idx = gather_idx.data_ptr() if gather_idx is not None else None
+    args.block_row_start = meta.block_row_start.data_ptr()
+    args.block_row_count = meta.block_row_count.data_ptr()
+    args.total_blocks = int(meta.total_blocks)
+    args.scales = scales.data_ptr()
+    kernel_q = None
+    if mode == LAYOUT_MODE_PADDED:
+        q_rows = int(meta.padded_rows)
+        pitch = operand_pitch(q_rows)
+        storage = torch.empty((n, pitch), device=dev, dtype=torch.float8_e4m3fn)
+        if pitch > q_rows:
+            storage[:, q_rows:].view(torch.uint8).zero_()
+        args.q_row_start = None           # row 128 b + k
+        args.q_zero_fill = 1              # rows past each block's count are zero
+    else:
+        assert mode == LAYOUT_MODE_PACKED
+        # reference quant.py:211-247: compact logical data on valid rows (128-byte
+        # K pitch) plus the zero-initialised launch copy with its TMA guard rows.
+        q_rows = int(meta.valid_rows)
+        pitch = operand_pitch(q_rows)
+        storage = torch.empty((n, pitch), device=dev, dtype=torch.float8_e4m3fn)
+        kernel_rows = packed_kernel_data_storage_rows(meta)
+        aligned_k = max(16, (kernel_rows + 15) // 16 * 16)
+        kernel_q = torch.zeros((n, aligned_k), device=dev, dtype=torch.float8_e4m3fn)
+        args.q_row_start = meta.block_row_start.data_ptr()
+        args.q_zero_fill = 0
+        args.kq_data = kernel_q.data_ptr()
+        args.kq_pitch = aligned_k
+        args.kq_row_start = packed_kernel_data_block_row_start(meta).data_ptr()
+    args.q_data = storage.data_ptr()
+    args.q_pitch = pitch
+    q = storage.as_strided((q_rows, n), (1, pitch))
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream().cuda_stream
+        _lib.check(lib.sm100_wgrad_quantize_1x128_ex(ctypes.byref(args), stream), "sm100_wgrad_quantize_1x128_ex")
+    return Fp8GroupedWgradOperand(q, scales, kernel_data=kernel_q)
+
+
 def quantize_grouped_wgrad_operand_128x1(
     x_grouped: torch.Tensor,
     meta: WgradScaleBlockMeta,
@@ -95,49 +160,41 @@ def quantize_grouped_wgrad_operand_128x1(
     layout_mode: str | None = None,
 ) -> Fp8GroupedWgradOperand:
     """Quantise expert-major grouped rows [valid_rows, cols] (BF16 or fp32)
-    into the padded FP8 operand layout with 1x128 fp32 scales.
+    into an FP8 operand with 1x128 fp32 scales (reference quant.py:175-270).
 
-    ``block_n`` is accepted for signature compatibility (the CUDA kernel tiles
-    64 columns per CTA).
+    ``layout_mode`` "padded" stores each expert in whole 128-row slots
+    (zero-filled tails); "packed" stores ``data`` on the valid rows only and a
+    launch copy ``kernel_data`` [cols, K] at the packed tail policy's block
+    starts (``wgmma_block_row_start`` for masked128) with its guard rows, as
+    the reference does. ``block_n`` is accepted for signature compatibility
+    (the CUDA kernel tiles 64 columns per CTA).
     """
     del block_n
-    if x_grouped.ndim != 2:
-        raise RuntimeError(f"expected x_grouped [valid_TK,N], got {tuple(x_grouped.shape)}")
-    if not x_grouped.is_cuda:
-        raise RuntimeError("x_grouped must be CUDA")
-    if x_grouped.dtype not in (torch.bfloat16, torch.float32):
-        raise RuntimeError(f"x_grouped must be bf16 or fp32, got {x_grouped.dtype}")
-    if not x_grouped.is_contiguous():
-        x_grouped = x_grouped.contiguous()
-    valid_tk, n = map(int, x_grouped.shape)
-    if int(meta.valid_rows) != valid_tk:
-        raise RuntimeError("meta.cu_seqlens_k[-1] must match x_grouped rows")
-    if int(meta.padded_rows) != int(meta.total_blocks) * int(meta.block_k):
-        raise RuntimeError("metadata padded_rows must equal total_blocks * block_k")
-    mode = resolve_wgrad_layout_mode(layout_mode)
-    if mode == LAYOUT_MODE_PACKED:
-        raise RuntimeError("packed layout is not implemented by the B200 engine yet; use layout_mode='padded'")
-    assert mode == LAYOUT_MODE_PADDED
+    return _quantize(x_grouped, None, meta, layout_mode)
 
-    q_rows = int(meta.padded_rows)
-    pitch = operand_pitch(q_rows)
-    storage = torch.empty((n, pitch), device=x_grouped.device, dtype=torch.float8_e4m3fn)
-    if pitch > q_rows:
-        storage[:, q_rows:].view(torch.uint8).zero_()
-    q = storage.as_strided((q_rows, n), (1, pitch))
-    scales = torch.empty((int(meta.total_blocks), n), device=x_grouped.device, dtype=torch.float32)
-    lib = _lib.load()
-    with torch.cuda.device(x_grouped.device):
-        stream = torch.cuda.current_stream().cuda_stream
-        _lib.check(
-            lib.sm100_wgrad_quantize_1x128(
-                x_grouped.data_ptr(), 0 if x_grouped.dtype == torch.bfloat16 else 1, valid_tk, n,
-                meta.block_row_start.data_ptr(), meta.block_row_count.data_ptr(), int(meta.total_blocks),
-                storage.data_ptr(), pitch, scales.data_ptr(), stream,
-            ),
-            "sm100_wgrad_quantize_1x128",
-        )
-    return Fp8GroupedWgradOperand(q, scales, kernel_data=None)
+
+def quantize_grouped_wgrad_operand_128x1_gather(
+    x: torch.Tensor,
+    gather_idx: torch.Tensor,
+    meta: WgradScaleBlockMeta,
+    *,
+    layout_mode: str | None = None,
+) -> Fp8GroupedWgradOperand:
+    """Gather + quantise in one pass: row r of the expert-major operand is row
+    ``gather_idx[r]`` of the token-major activation ``x`` [tokens, cols].
+
+    Equal, byte for byte, to ``quantize_grouped_wgrad_operand_128x1(x[gather_idx], meta)``
+    without materialising the grouped BF16 copy (the reference harness builds
+    it with a separate gather, synthetic.py:132-150 and :243-244).
+    """
+    if gather_idx.ndim != 1 or not gather_idx.is_cuda:
+        raise RuntimeError("gather_idx must be a 1-D CUDA tensor")
+    if int(gather_idx.numel()) != int(meta.valid_rows):
+        raise RuntimeError(f"gather_idx has {int(gather_idx.numel())} rows, metadata {int(meta.valid_rows)}")
+    if gather_idx.device != x.device:
+        raise RuntimeError("gather_idx and x must be on the same device")
+    idx = gather_idx if gather_idx.dtype == torch.int32 else gather_idx.to(torch.int32)
+    return _quantize(x, idx.contiguous(), meta, layout_mode)
 
 
 def quantize_grouped_wgrad_operand_tail_k(
