@@ -131,7 +131,8 @@ def flops_of(inp) -> tuple[float, float]:
 def hbm_bytes_of(inp) -> float:
     """Algorithmic HBM bytes of one step: FP8 operands, fp32 scales, BF16 outputs."""
     h, i, e = inp.hidden, inp.intermediate, inp.experts
-    pad = inp.meta.padded_rows
+    # operand rows the GEMM streams: 128-row slots (padded) or 32-row-aligned segments (packed)
+    pad = inp.meta.wgmma_rows if inp.grad_y_q.kernel_data is not None else inp.meta.padded_rows
     blocks = inp.meta.total_blocks
     return float(pad * (2 * h + 3 * i) + blocks * (2 * h + 3 * i) * 4 + e * 3 * h * i * 2)
 
@@ -220,10 +221,10 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def workload_config(workload: str, world: int) -> dict:
+def workload_config(workload: str, world: int, layout: str = "padded") -> dict:
     e_all, top_k, h, i, t, route = WORKLOADS[workload]
     return {"workload": workload, "experts": e_all, "top_k": top_k, "hidden": h, "intermediate": i,
-            "tokens": t, "route": route, "parallelism": f"ep{world}", "layout": "padded",
+            "tokens": t, "route": route, "parallelism": f"ep{world}", "layout": layout,
             "l2": "inputs larger than L2 (no flush needed)" if workload not in ("tiny",) else "flush"}
 
 
@@ -284,7 +285,8 @@ def run_ours(args) -> None:
     e0, e1 = shard_experts(e_all, world, rank)
     t_setup = time.perf_counter()
     inp = make_synthetic_wgrad_inputs(tokens=t, experts=e_all, top_k=top_k, hidden=h, intermediate=i, route=route,
-                                      seed=args.seed, device=dev, expert_range=(e0, e1), routing=routing)
+                                      seed=args.seed, device=dev, expert_range=(e0, e1), routing=routing,
+                                      layout_mode=args.layout)
     inp.drop_sources()
     torch.cuda.empty_cache()
     torch.cuda.synchronize(dev)
@@ -381,7 +383,7 @@ def run_ours(args) -> None:
             "vs_baseline_ref": "reference sm90 kernel on H100, same per-GPU problem (BASELINE.md)",
             "dtype": "fp8e4m3->f32acc->bf16",
             "data": "synthetic",
-            "config": workload_config(args.workload, world),
+            "config": workload_config(args.workload, world, args.layout),
             "stages_ms": {"down": down_ms, "gate_up": gate_ms},
             "stages_tflops": {"down": down_flops_tf, "gate_up": gate_flops_tf},
             "pct_of_fp8_peak": value / world / fp8_peak,
@@ -408,11 +410,14 @@ def run_e2e(inp, args, world, dev, step_flops) -> dict:
 
     dev_inputs = []
     for op in (inp.grad_y_q, inp.hidden_q, inp.grad_gate_up_q, inp.x_q):
-        pitch = op.data.stride(1)
-        storage = op.data.as_strided((op.data.shape[1], pitch), (pitch, 1))
+        if op.kernel_data is not None:        # packed layout: the launch copy is what the GEMM reads
+            storage = op.kernel_data
+        else:
+            pitch = op.data.stride(1)
+            storage = op.data.as_strided((op.data.shape[1], pitch), (pitch, 1))
         dev_inputs += [storage, op.scales]
     m = inp.meta
-    dev_inputs += [m.padded_cu_seqlens_k, m.block_offsets, m.expert_order]
+    dev_inputs += [m.padded_cu_seqlens_k, m.wgmma_cu_seqlens_k, m.block_offsets, m.expert_order]
     outs = [inp.down_out_bf16, inp.gate_up_out_bf16]
 
     def pinned_like(t):
@@ -462,6 +467,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="dsv3_32k")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--layout", choices=("padded", "packed"), default="padded",
+                    help="operand layout (KERNEL_LAB_WGRAD_LAYOUT_MODE of the reference)")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
