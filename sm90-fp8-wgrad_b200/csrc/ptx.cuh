@@ -73,6 +73,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return ok != 0;
 }
 
+// Non-blocking probe of two barriers at once: both test_wait instructions are
+// in flight together, so the common case (both phases already complete) costs
+// one shared-memory round trip instead of two.
+__device__ __forceinline__ bool mbar_test2(uint32_t a1, uint32_t p1, uint32_t a2, uint32_t p2) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 q, [%3], %4;\n\t"
+      "and.pred p, p, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(a1), "r"(p1), "r"(a2), "r"(p2)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with the given parity has completed. Returns false if
 // the wait gave up (timeout, or another role of this CTA already aborted).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
@@ -91,6 +108,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       }
     }
   }
+}
+
+// Wait for two barrier phases; both are probed together first.
+__device__ __forceinline__ bool mbar_wait2(uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2,
+                                           volatile int* abort_flag, unsigned int timeout_code) {
+  if (mbar_test2(smem_u32(b1), p1, smem_u32(b2), p2)) return true;
+  return mbar_wait(b1, p1, abort_flag, timeout_code) && mbar_wait(b2, p2, abort_flag, timeout_code);
 }
 
 // ---------------------------------------------------------------- TMA
@@ -173,6 +197,15 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// tcgen05.wait::ld, then re-define the destination registers of the loads it
+// waited for, so the compiler cannot schedule any use of them above the wait.
+template <int N>
+__device__ __forceinline__ void tmem_wait_ld_bind(uint32_t (&r)[N]) {
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
 
 // 32 lanes x 32 consecutive 32-bit columns: thread i of the warp receives lane
 // (taddr.lane + i), columns [taddr.col, taddr.col + 32).

@@ -64,7 +64,7 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BK;
   static constexpr int SCALE_FLOATS = BM + BN;
   static constexpr int COLS_PER_WARP = BN / 2;     // two column halves of 4 warps each
-  static constexpr int CHUNKS = COLS_PER_WARP / 16;  // tcgen05.ld x16 chunks
+  static constexpr int CHUNKS32 = COLS_PER_WARP / 32;  // tcgen05.ld x32 chunks
   static constexpr int TMEM_COLS = 2 * BN;          // double-buffered partial
   static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + NUM_EPI_WARPS * OUT_STAGE_BYTES_PER_WARP +
                                     SCALE_STAGES * SCALE_FLOATS * 4 + 256 /*barriers*/ + 1024 /*align*/;
@@ -201,8 +201,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int kb = 0; kb < nkb; ++kb) {
         const int atoms = kb + 1 == nkb ? last_atoms : BK / 32;
         // Whole warp waits (keeps the warp converged for the .sync.aligned ops).
-        ok = mbar_wait(&tempty_bar[acc], aphase ^ 1u, abort_flag, kDevTimeoutMma);
-        if (ok) ok = mbar_wait(&full_bar[stage], phase, abort_flag, kDevTimeoutMma);
+        ok = mbar_wait2(&tempty_bar[acc], aphase ^ 1u, &full_bar[stage], phase, abort_flag, kDevTimeoutMma);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
@@ -248,8 +247,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int j = 0; j < C::COLS_PER_WARP; ++j) fin[j] = 0.f;
 
       for (int kb = 0; kb < nkb; ++kb) {
-        ok = mbar_wait(&tfull_bar[acc], aphase, abort_flag, kDevTimeoutEpilogue);
-        if (ok) ok = mbar_wait(&sfull_bar[sstage], sphase, abort_flag, kDevTimeoutEpilogue);
+        ok = mbar_wait2(&tfull_bar[acc], aphase, &sfull_bar[sstage], sphase, abort_flag, kDevTimeoutEpilogue);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
@@ -257,28 +255,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const float a_s = sc[row];
         const float* b_s = sc + BM + half * C::COLS_PER_WARP;
         const uint32_t t_addr = tmem_base + lane_addr + static_cast<uint32_t>(acc * BN + half * C::COLS_PER_WARP);
+        // Software pipeline over 32-column chunks: the TMEM load of chunk c+1
+        // is in flight while chunk c is promoted. Once the last chunk is in
+        // registers the TMEM buffer goes back to the MMA warp, before its math.
+        uint32_t r[2][32];
+        tmem_ld_32x32b_x32(t_addr, r[0]);
 #pragma unroll
-        for (int c = 0; c < C::CHUNKS; ++c) {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(t_addr + c * 16, r);
-          tmem_wait_ld();
+        for (int c = 0; c < C::CHUNKS32; ++c) {
+          tmem_wait_ld_bind(r[c & 1]);
+          if (c + 1 < C::CHUNKS32) {
+            tmem_ld_32x32b_x32(t_addr + (c + 1) * 32, r[(c + 1) & 1]);
+          } else {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+          }
 #pragma unroll
-          for (int j = 0; j < 16; j += 4) {
-            const float4 sb4 = *reinterpret_cast<const float4*>(b_s + c * 16 + j);
+          for (int j = 0; j < 32; j += 4) {
+            const float4 sb4 = *reinterpret_cast<const float4*>(b_s + c * 32 + j);
+            const uint32_t* q = &r[c & 1][j];
             float u0, u1, u2, u3;
-            mul_f32x2(u0, u1, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), sb4.x, sb4.y);
-            mul_f32x2(u2, u3, __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]), sb4.z, sb4.w);
-            float* f = &fin[c * 16 + j];
+            mul_f32x2(u0, u1, __uint_as_float(q[0]), __uint_as_float(q[1]), sb4.x, sb4.y);
+            mul_f32x2(u2, u3, __uint_as_float(q[2]), __uint_as_float(q[3]), sb4.z, sb4.w);
+            float* f = &fin[c * 32 + j];
             fma_f32x2(f[0], f[1], u0, u1, a_s, a_s, f[0], f[1]);
             fma_f32x2(f[2], f[3], u2, u3, a_s, a_s, f[2], f[3]);
           }
         }
-        tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&tempty_bar[acc]);
-          mbar_arrive(&sempty_bar[sstage]);
-        }
+        if (lane == 0) mbar_arrive(&sempty_bar[sstage]);
         acc ^= 1;
         if (acc == 0) aphase ^= 1u;
         if (++sstage == SCALE_STAGES) { sstage = 0; sphase ^= 1u; }
