@@ -142,6 +142,10 @@ typedef struct Sm100WgradQuantArgs {
   int64_t kq_pitch;
   const int32_t* kq_row_start;    /* [total_blocks], required with kq_data                */
   float* scales;                  /* [total_blocks][cols]                                 */
+  int32_t block_rows;             /* rows per scale block: 128 (0 means 128), or 32 / 64 for
+                                     the compact tail operands of quant.py:273-307        */
+  int64_t x_rows;                 /* rows of x; required with gather_idx (an index outside
+                                     [0, x_rows) reads zeros and sets device error 5)      */
 } Sm100WgradQuantArgs;
 
 SM100_WGRAD_API int sm100_wgrad_quantize_1x128_ex(const Sm100WgradQuantArgs* args, void* stream);
@@ -181,7 +185,9 @@ SM100_WGRAD_API int sm100_wgrad_build_meta(const int32_t* cu_seqlens_k, int64_t 
 
 /* Reads and clears the device error word of the current device (synchronous;
  * diagnostics only, never call it inside a timed region). Writes one of the
- * device error codes (0 = none) to *code. */
+ * device error codes to *code: 0 none; 1, 2, 3 a bounded wait of the GEMM's
+ * producer, MMA or epilogue role expired; 4 bad tile; 5 a quantiser gather
+ * index outside [0, x_rows). The first error since the last read is kept. */
 SM100_WGRAD_API int sm100_wgrad_device_error(int32_t* code);
 
 /* Human-readable text of a status code (static storage). */

@@ -186,25 +186,34 @@ class OracleOperand:
         return e4m3_decode(self.data[:, b * BLOCK_K : b * BLOCK_K + rows]).T
 
 
-def quantize_1x128(x: np.ndarray, meta: OracleMeta) -> OracleOperand:
-    """quant.py:129-167 (padded layout, dst row = 128 b + k), quant.py:222-247
-    (pitch = max(128, ceil(K/128)*128), padded rows zero)."""
+def quantize_blocks(x: np.ndarray, block_row_start, block_row_count, block_k: int, padded_rows: int) -> OracleOperand:
+    """quant.py:129-167 for any scale-block height (the kernel's BLOCK_K is
+    meta.block_k, quant.py:258): block b's valid rows are quantised with
+    per-column amax/448 scales into padded rows block_k * b + k (quant.py:139),
+    pitch = max(128, ceil(K/128)*128) and padded rows zero (quant.py:222-247)."""
     x = np.asarray(x, dtype=np.float32)
-    if x.ndim != 2 or x.shape[0] != meta.valid_rows:
-        raise RuntimeError("x must be [valid_rows, cols]")
     cols = x.shape[1]
-    pitch = max(BLOCK_K, (meta.padded_rows + BLOCK_K - 1) // BLOCK_K * BLOCK_K)
+    nblocks = len(block_row_start)
+    pitch = max(BLOCK_K, (padded_rows + BLOCK_K - 1) // BLOCK_K * BLOCK_K)
     data = np.zeros((cols, pitch), dtype=np.uint8)
-    scales = np.empty((meta.total_blocks, cols), dtype=np.float32)
-    for b in range(meta.total_blocks):
-        r0, n = int(meta.block_row_start[b]), int(meta.block_row_count[b])
+    scales = np.empty((nblocks, cols), dtype=np.float32)
+    for b in range(nblocks):
+        r0, n = int(block_row_start[b]), int(block_row_count[b])
         blk = x[r0 : r0 + n]                                         # valid rows only (mask k < row_count)
         amax = np.abs(blk).max(axis=0) if n else np.zeros(cols, np.float32)
         scale = np.maximum((amax / FP8_MAX).astype(np.float32), SCALE_EPS)  # fp32 division, eps floor
         scales[b] = scale
         q = (blk / scale[None, :]).astype(np.float32)                # x / scale, fp32
-        data[:, b * BLOCK_K : b * BLOCK_K + n] = e4m3_encode(q).T
-    return OracleOperand(data=data, scales=scales, k_rows=meta.padded_rows)
+        data[:, b * block_k : b * block_k + n] = e4m3_encode(q).T
+    return OracleOperand(data=data, scales=scales, k_rows=padded_rows)
+
+
+def quantize_1x128(x: np.ndarray, meta: OracleMeta) -> OracleOperand:
+    """The padded 128-row operand (quant.py:129-167, :222-247)."""
+    x = np.asarray(x, dtype=np.float32)
+    if x.ndim != 2 or x.shape[0] != meta.valid_rows:
+        raise RuntimeError("x must be [valid_rows, cols]")
+    return quantize_blocks(x, meta.block_row_start, meta.block_row_count, BLOCK_K, meta.padded_rows)
 
 
 _PACKED_GUARD_ROWS = {"masked128": 127, "adaptive64": 63, "adaptive32_64_128": 127, "adaptive32_64_twophase": 31}

@@ -17,7 +17,7 @@ cudaError_t launch_quantize_1x128(const void* x, int x_dtype, int64_t cols, cons
                                   const int32_t* block_row_start, const int32_t* block_row_count,
                                   int64_t total_blocks, void* q, int64_t q_pitch, const int32_t* q_row_start,
                                   bool q_zero_fill, void* kq, int64_t kq_pitch, const int32_t* kq_row_start,
-                                  float* scales, cudaStream_t stream);
+                                  float* scales, int block_rows, int64_t x_rows, cudaStream_t stream);
 cudaError_t launch_build_meta(const int32_t* cu, int64_t num_experts, const Sm100WgradMetaOut& out,
                               cudaStream_t stream);
 }  // namespace wgrad
@@ -222,7 +222,7 @@ int sm100_wgrad_quantize_1x128(const void* x, int32_t x_dtype, int64_t valid_row
   if (st != SM100_WGRAD_OK) return st;
   const cudaError_t err = wgrad::launch_quantize_1x128(x, x_dtype, cols, nullptr, block_row_start, block_row_count,
                                                        total_blocks, q_data, q_pitch, nullptr, true, nullptr, 0,
-                                                       nullptr, scales, static_cast<cudaStream_t>(stream));
+                                                       nullptr, scales, 128, valid_rows, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? SM100_WGRAD_OK : SM100_WGRAD_ERR_LAUNCH;
 }
 
@@ -234,7 +234,10 @@ int sm100_wgrad_quantize_1x128_ex(const Sm100WgradQuantArgs* a, void* stream) {
   if (a->x == nullptr || a->block_row_start == nullptr || a->block_row_count == nullptr || a->q_data == nullptr ||
       a->scales == nullptr)
     return SM100_WGRAD_ERR_INVALID_ARG;
-  if (a->q_row_start == nullptr && (a->q_pitch < a->total_blocks * 128 || a->q_pitch % 16 != 0))
+  const int block_rows = a->block_rows == 0 ? 128 : a->block_rows;
+  if (block_rows != 32 && block_rows != 64 && block_rows != 128) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->gather_idx != nullptr && a->x_rows <= 0) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->q_row_start == nullptr && (a->q_pitch < a->total_blocks * block_rows || a->q_pitch % 16 != 0))
     return SM100_WGRAD_ERR_INVALID_ARG;
   if (a->kq_data != nullptr && a->kq_row_start == nullptr) return SM100_WGRAD_ERR_INVALID_ARG;
   if (a->total_blocks > INT32_MAX) return SM100_WGRAD_ERR_UNSUPPORTED;
@@ -244,7 +247,7 @@ int sm100_wgrad_quantize_1x128_ex(const Sm100WgradQuantArgs* a, void* stream) {
   const cudaError_t err = wgrad::launch_quantize_1x128(
       a->x, a->x_dtype, a->cols, a->gather_idx, a->block_row_start, a->block_row_count, a->total_blocks, a->q_data,
       a->q_pitch, a->q_row_start, a->q_zero_fill != 0, a->kq_data, a->kq_pitch, a->kq_row_start, a->scales,
-      static_cast<cudaStream_t>(stream));
+      block_rows, a->x_rows, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? SM100_WGRAD_OK : SM100_WGRAD_ERR_LAUNCH;
 }
 

@@ -24,6 +24,7 @@ enum DeviceError : unsigned int {
   kDevTimeoutMma = 2,
   kDevTimeoutEpilogue = 3,
   kDevBadTile = 4,
+  kDevBadGatherIndex = 5,  // quantiser gather index outside [0, x_rows)
 };
 
 // Module-global device error word (read and cleared by sm100_wgrad_device_error).

@@ -19,6 +19,10 @@
 // token-major activation (row r of the grouped operand = x row gather_idx[r]),
 // which fuses the expert-major gather of the MoE backward into the quantiser.
 //
+// Scale blocks are 128 rows (the GEMM's contract) or, for the reference's
+// compact tail operands (quant.py:273-307), 32 or 64 rows: block b then
+// occupies padded rows [block_rows * b, block_rows * (b + 1)).
+//
 // HBM-bound transpose: a CTA reads a 128-row x 64-column BF16 tile with
 // 16-byte coalesced loads, reduces column amax through shared memory and
 // writes each column's 128 FP8 bytes as one contiguous 128-byte segment
@@ -28,6 +32,8 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+
+#include "ptx.cuh"
 
 namespace wgrad {
 
@@ -88,7 +94,8 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
                                                                   const int32_t* __restrict__ block_row_start,
                                                                   const int32_t* __restrict__ block_row_count,
                                                                   QuantDst d0, QuantDst d1,
-                                                                  float* __restrict__ scales, bool vec_ok) {
+                                                                  float* __restrict__ scales, bool vec_ok,
+                                                                  int block_rows, int64_t x_rows) {
   __shared__ float tile[QBLOCK_ROWS][QBLOCK_COLS + 1];
   __shared__ float s_amax[4][QBLOCK_COLS];
   __shared__ float s_scale[QBLOCK_COLS];
@@ -110,9 +117,17 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
       const int r = pass * 32 + r_in;
       float v[8];
       if (r < rows && cc < ncols) {
-        const int64_t xrow = gather_idx != nullptr ? static_cast<int64_t>(__ldg(gather_idx + row0 + r)) : row0 + r;
-        const T* src = x + xrow * cols + c0 + cc;
-        if (vec_ok && cc + 8 <= ncols) {
+        int64_t xrow = gather_idx != nullptr ? static_cast<int64_t>(__ldg(gather_idx + row0 + r)) : row0 + r;
+        if (gather_idx != nullptr && (xrow < 0 || xrow >= x_rows)) {
+          // Out-of-range gather index: read nothing, flag the device error word.
+          record_device_error(kDevBadGatherIndex);
+          xrow = -1;
+        }
+        const T* src = x + (xrow < 0 ? 0 : xrow) * cols + c0 + cc;
+        if (xrow < 0) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = 0.f;
+        } else if (vec_ok && cc + 8 <= ncols) {
           load8<T>(src, v);
         } else {
 #pragma unroll
@@ -170,8 +185,9 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
       const QuantDst& d = o == 0 ? d0 : d1;
       if (d.q == nullptr) continue;
       const int64_t start = d.row_start != nullptr ? static_cast<int64_t>(__ldg(d.row_start + b))
-                                                   : static_cast<int64_t>(b) * QBLOCK_ROWS;
-      const int limit = d.zero_fill ? QBLOCK_ROWS : rows;  // rows k < limit are written
+                                                   : static_cast<int64_t>(b) * block_rows;
+      const int limit = d.zero_fill ? block_rows : rows;  // rows k < limit are written
+      if (chunk * 16 >= limit) continue;
       uint8_t* dst = d.q + (c0 + col) * d.pitch + start + chunk * 16;
       if (chunk * 16 + 16 <= limit && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
         *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -188,7 +204,7 @@ cudaError_t launch_quantize_1x128(const void* x, int x_dtype, int64_t cols, cons
                                   const int32_t* block_row_start, const int32_t* block_row_count,
                                   int64_t total_blocks, void* q, int64_t q_pitch, const int32_t* q_row_start,
                                   bool q_zero_fill, void* kq, int64_t kq_pitch, const int32_t* kq_row_start,
-                                  float* scales, cudaStream_t stream) {
+                                  float* scales, int block_rows, int64_t x_rows, cudaStream_t stream) {
   if (total_blocks == 0 || cols == 0) return cudaSuccess;
   const dim3 grid(static_cast<unsigned>(total_blocks), static_cast<unsigned>((cols + QBLOCK_COLS - 1) / QBLOCK_COLS));
   const QuantDst d0{static_cast<uint8_t*>(q), q_pitch, q_row_start, q_zero_fill};
@@ -197,12 +213,12 @@ cudaError_t launch_quantize_1x128(const void* x, int x_dtype, int64_t cols, cons
     const bool vec_ok = (cols % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
     quantize_1x128_kernel<__nv_bfloat16><<<grid, QTHREADS, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(x), cols, gather_idx, block_row_start, block_row_count, d0, d1, scales,
-        vec_ok);
+        vec_ok, block_rows, x_rows);
   } else {
     const bool vec_ok = (cols % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
     quantize_1x128_kernel<float><<<grid, QTHREADS, 0, stream>>>(static_cast<const float*>(x), cols, gather_idx,
                                                                block_row_start, block_row_count, d0, d1, scales,
-                                                               vec_ok);
+                                                               vec_ok, block_rows, x_rows);
   }
   return cudaGetLastError();
 }

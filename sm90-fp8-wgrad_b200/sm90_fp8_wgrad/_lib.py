@@ -85,6 +85,8 @@ class Sm100WgradQuantArgs(ctypes.Structure):
         ("kq_pitch", ctypes.c_int64),
         ("kq_row_start", ctypes.c_void_p),
         ("scales", ctypes.c_void_p),
+        ("block_rows", ctypes.c_int32),
+        ("x_rows", ctypes.c_int64),
     ]
 
 

@@ -107,6 +107,11 @@ def _quantize(x: torch.Tensor, gather_idx: torch.Tensor | None, meta: WgradScale
     if int(meta.padded_rows) != int(meta.total_blocks) * int(meta.block_k):
         raise RuntimeError("metadata padded_rows must equal total_blocks * block_k")
     mode = resolve_wgrad_layout_mode(layout_mode)
+    block_rows = int(meta.block_k)
+    if block_rows not in (32, 64, 128):
+        raise RuntimeError(f"meta.block_k must be 32, 64 or 128, got {block_rows}")
+    if block_rows != 128 and mode != LAYOUT_MODE_PADDED:
+        raise RuntimeError("32/64-row scale blocks use the padded layout")
     dev = x.device
     scales = torch.empty((int(meta.total_blocks), n), device=dev, dtype=torch.float32)
     args = _lib.Sm100WgradQuantArgs()
@@ -118,6 +123,8 @@ def _quantize(x: torch.Tensor, gather_idx: torch.Tensor | None, meta: WgradScale
     args.block_row_count = meta.block_row_count.data_ptr()
     args.total_blocks = int(meta.total_blocks)
     args.scales = scales.data_ptr()
+    args.block_rows = block_rows
+    args.x_rows = int(x.shape[0])
     kernel_q = None
     if mode == LAYOUT_MODE_PADDED:
         q_rows = int(meta.padded_rows)
@@ -204,11 +211,30 @@ def quantize_grouped_wgrad_operand_tail_k(
     *,
     block_n: int = 32,
 ) -> Fp8GroupedWgradOperand:
-    """Quantise compact per-expert tail rows (reference quant.py:273-307)."""
+    """Quantise compact per-expert tail rows (reference quant.py:273-307).
+
+    Row r of the compact tail operand is row ``tail_indices[r]`` of the
+    expert-major ``x_grouped``; it is quantised with ``tail_meta.block_k``-row
+    (32 or 64) scale blocks into the padded layout, block b at rows
+    [block_k * b, block_k * (b + 1)). The reference gathers with
+    ``index_select`` and then quantises; here the gather is fused into the
+    quantiser's loads. An index outside ``x_grouped`` reads zeros and sets
+    device error 5 (``sm100_wgrad_device_error``) instead of faulting.
+    """
+    del block_n
     if tail_indices.ndim != 1:
         raise RuntimeError(f"expected tail_indices [tail_rows], got {tuple(tail_indices.shape)}")
     if not tail_indices.is_cuda:
         raise RuntimeError("tail_indices must be CUDA")
     if int(tail_meta.block_k) not in (32, 64):
         raise RuntimeError(f"tail_meta.block_k must be 32 or 64, got {tail_meta.block_k}")
-    raise RuntimeError("tail_k operands use 32/64-row scale blocks, which the B200 engine does not run")
+    if x_grouped.ndim != 2:
+        raise RuntimeError(f"expected x_grouped [valid_TK,N], got {tuple(x_grouped.shape)}")
+    if not x_grouped.is_cuda:
+        raise RuntimeError("x_grouped must be CUDA")
+    if int(tail_meta.valid_rows) != int(tail_indices.numel()):
+        raise RuntimeError("tail_meta.valid_rows must match compact tail source rows")
+    if tail_indices.device != x_grouped.device:
+        raise RuntimeError("tail_indices and x_grouped must be on the same device")
+    idx = tail_indices if tail_indices.dtype == torch.int32 else tail_indices.to(torch.int32)
+    return _quantize(x_grouped, idx.contiguous(), tail_meta, LAYOUT_MODE_PADDED)
