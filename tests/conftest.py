@@ -38,3 +38,12 @@ def cuda_device():
     if (major, minor) != (10, 0):
         pytest.skip(f"needs compute capability 10.0, got {major}.{minor}")
     return torch.device("cuda:0")
+
+
+@pytest.fixture(autouse=True)
+def _isolated_layout_mode(monkeypatch):
+    """Every test starts without KERNEL_LAB_WGRAD_LAYOUT_MODE and gets the
+    caller's value back afterwards: the synthetic-input builder sets it for the
+    whole process, as the reference harness does (synthetic.py:218)."""
+    monkeypatch.delenv("KERNEL_LAB_WGRAD_LAYOUT_MODE", raising=False)
+    yield
