@@ -53,10 +53,15 @@ extern "C" {
 #define SM100_WGRAD_OUT_BF16 0
 #define SM100_WGRAD_OUT_F32 1
 
-/* Tile configurations selectable through Sm100WgradArgs.tile_config. */
+/* Tile configurations selectable through Sm100WgradArgs.tile_config.
+ * AUTO picks the N width by shape; AUTO and 128x256 pick the number of
+ * promotion warps of the 256-wide tile by K depth (16 when the experts average
+ * few 128-row blocks, 8 otherwise); the _W8 / _W16 forms force it. */
 #define SM100_WGRAD_TILE_AUTO 0
 #define SM100_WGRAD_TILE_128x256 1
 #define SM100_WGRAD_TILE_128x128 2
+#define SM100_WGRAD_TILE_128x256_W8 3
+#define SM100_WGRAD_TILE_128x256_W16 4
 
 typedef struct Sm100WgradArgs {
   const void* lhs_data;      /* FP8 e4m3 [M][lhs_pitch]                              */

@@ -112,10 +112,23 @@ int encode_out_map(CUtensorMap* map, void* out, int out_f32, int64_t e, int64_t 
 
 int pick_bn(int32_t tile_config, int64_t n) {
   if (tile_config == SM100_WGRAD_TILE_128x128) return 128;
-  if (tile_config == SM100_WGRAD_TILE_128x256) return 256;
+  if (tile_config == SM100_WGRAD_TILE_128x256 || tile_config == SM100_WGRAD_TILE_128x256_W8 ||
+      tile_config == SM100_WGRAD_TILE_128x256_W16)
+    return 256;
   // auto: the wide tile halves operand re-reads per output byte; a narrow N
   // would only fill it with zero columns.
   return n <= 128 ? 128 : 256;
+}
+
+// Average 128-row K blocks per expert at or below which the 256-wide tile runs
+// 16 promotion warps: such launches are bound by output stores and per-block
+// latency, which more warps overlap; deeper K favours 8 warps.
+constexpr int64_t kShortKBlocksPerExpert = 2;
+
+int pick_epi_warps(int32_t tile_config, int bn, int64_t total_blocks, int64_t num_experts) {
+  if (bn != 256 || tile_config == SM100_WGRAD_TILE_128x256_W8) return 8;
+  if (tile_config == SM100_WGRAD_TILE_128x256_W16) return 16;
+  return total_blocks <= kShortKBlocksPerExpert * num_experts ? 16 : 8;
 }
 
 }  // namespace
@@ -143,8 +156,7 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   if (a->num_experts < 0 || a->m <= 0 || a->n <= 0 || a->k_rows < 0 || a->total_blocks < 0)
     return SM100_WGRAD_ERR_INVALID_ARG;
   if (a->out_dtype != SM100_WGRAD_OUT_BF16 && a->out_dtype != SM100_WGRAD_OUT_F32) return SM100_WGRAD_ERR_INVALID_ARG;
-  if (a->tile_config != SM100_WGRAD_TILE_AUTO && a->tile_config != SM100_WGRAD_TILE_128x256 &&
-      a->tile_config != SM100_WGRAD_TILE_128x128)
+  if (a->tile_config < SM100_WGRAD_TILE_AUTO || a->tile_config > SM100_WGRAD_TILE_128x256_W16)
     return SM100_WGRAD_ERR_INVALID_ARG;
   // TMA: output row pitch and scale-vector chunks must be 16-byte multiples.
   if (a->m % 16 != 0 || a->n % 16 != 0) return SM100_WGRAD_ERR_UNSUPPORTED;
@@ -198,6 +210,7 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   p.out_f32 = a->out_dtype == SM100_WGRAD_OUT_F32;
   p.accumulate = a->accumulate != 0;
   p.has_operands = has_operands ? 1 : 0;
+  p.epi_warps = pick_epi_warps(a->tile_config, bn, a->total_blocks, a->num_experts);
 
   int grid = info.sm_count;
   if (a->max_ctas > 0 && a->max_ctas < grid) grid = a->max_ctas;

@@ -50,25 +50,41 @@ constexpr int BM = 128;
 constexpr int BK = 128;  // scale block == K block, bytes per row of an FP8 tile
 constexpr int STAGES = 3;
 constexpr int SCALE_STAGES = 6;
-constexpr int NUM_EPI_WARPS = 8;
-constexpr int NUM_THREADS = 32 * (4 + NUM_EPI_WARPS);  // warpgroup 0: TMA, MMA, 2 idle; warpgroups 1-2: epilogue
 constexpr int FIRST_EPI_WARP = 4;
-// Register split (launch: 65536 / 384 = 168 per thread): 128 x 56 + 256 x 224 = 64512.
-constexpr uint32_t REGS_CONTROL = 56;
-constexpr uint32_t REGS_EPILOGUE = 224;
-constexpr int OUT_STAGE_BYTES_PER_WARP = 8192;
 
-template <int BN>
+// Promotion warps: EPI = 8 or 16 (two or four per TMEM lane quarter); each owns
+// 32 rows x BN / (EPI / 4) columns. 16 warps keep more TMEM loads, scale loads
+// and output stores in flight (better for short-K, HBM-bound launches); 8 warps
+// carry fewer per-warp fixed costs (better for long K).
+// Register split: the launch gives THREADS x (65536 / THREADS rounded down to
+// 8) registers; warpgroup 0 drops to REGS_CONTROL and the promotion warps take
+// the rest: 16 warps: 640 x 96 = 128 x 32 + 512 x 112;
+//            8 warps: 384 x 168 >= 128 x 56 + 256 x 224.
+template <int BN, int EPI>
 struct Cfg {
+  static constexpr int EPI_WARPS = EPI;
+  static constexpr int THREADS = 32 * (4 + EPI_WARPS);
+  static constexpr uint32_t REGS_CONTROL = EPI_WARPS == 16 ? 32 : 56;
+  static constexpr uint32_t REGS_EPILOGUE = EPI_WARPS == 16 ? 112 : 224;
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int SCALE_FLOATS = BM + BN;
-  static constexpr int COLS_PER_WARP = BN / 2;     // two column halves of 4 warps each
-  static constexpr int CHUNKS32 = COLS_PER_WARP / 32;  // tcgen05.ld x32 chunks
+  static constexpr int COLS_PER_WARP = BN / (EPI_WARPS / 4);  // EPI_WARPS / 4 column groups
+  static constexpr int CHUNK = COLS_PER_WARP >= 128 ? 32 : 16;  // tcgen05.ld columns per load
+  static constexpr int CHUNKS = COLS_PER_WARP / CHUNK;
+  static constexpr int OUT_STAGE_BYTES_PER_WARP = COLS_PER_WARP * 32 * 2 >= 8192 ? 8192 : 4096;
   static constexpr int TMEM_COLS = 2 * BN;          // double-buffered partial
-  static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + NUM_EPI_WARPS * OUT_STAGE_BYTES_PER_WARP +
+  static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + EPI_WARPS * OUT_STAGE_BYTES_PER_WARP +
                                     SCALE_STAGES * SCALE_FLOATS * 4 + 256 /*barriers*/ + 1024 /*align*/;
+  static_assert(128 * REGS_CONTROL + 32 * EPI_WARPS * REGS_EPILOGUE <= THREADS * ((65536 / THREADS) & ~7),
+                "register split exceeds the launch allocation");
 };
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, uint32_t (&r)[N]) {
+  if constexpr (N == 32) tmem_ld_32x32b_x32(taddr, r);
+  else tmem_ld_32x32b_x16(taddr, r);
+}
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -95,17 +111,17 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, int tile) 
   return c;
 }
 
-template <int BN>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+template <int BN, int EPI>
+__global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
     grouped_wgrad_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                          const __grid_constant__ CUtensorMap tmap_out, const GemmParams p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
   uint8_t* s_b = s_a + STAGES * C::A_BYTES;
   uint8_t* s_out = s_b + STAGES * C::B_BYTES;
-  float* s_scale = reinterpret_cast<float*>(s_out + NUM_EPI_WARPS * OUT_STAGE_BYTES_PER_WARP);
+  float* s_scale = reinterpret_cast<float*>(s_out + C::EPI_WARPS * C::OUT_STAGE_BYTES_PER_WARP);
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_scale + SCALE_STAGES * C::SCALE_FLOATS);
   uint64_t* full_bar = bars;                          // [STAGES]   TMA -> MMA
   uint64_t* empty_bar = full_bar + STAGES;            // [STAGES]   MMA -> TMA
@@ -126,11 +142,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int i = 0; i < SCALE_STAGES; ++i) {
       mbar_init(&sfull_bar[i], 1);
-      mbar_init(&sempty_bar[i], NUM_EPI_WARPS);
+      mbar_init(&sempty_bar[i], C::EPI_WARPS);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull_bar[i], 1);
-      mbar_init(&tempty_bar[i], NUM_EPI_WARPS);
+      mbar_init(&tempty_bar[i], C::EPI_WARPS);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -149,7 +165,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
-  if (warp < FIRST_EPI_WARP) setmaxnreg_dec<REGS_CONTROL>();
+  if (warp < FIRST_EPI_WARP) setmaxnreg_dec<C::REGS_CONTROL>();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -227,13 +243,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp >= FIRST_EPI_WARP) {
     // ------------------------------------------------------------ promotion + epilogue
-    setmaxnreg_inc<REGS_EPILOGUE>();
-    const int ew = warp - FIRST_EPI_WARP;    // 0..7
+    setmaxnreg_inc<C::REGS_EPILOGUE>();
+    const int ew = warp - FIRST_EPI_WARP;    // 0 .. EPI_WARPS-1
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
-    const int half = ew >> 2;                // column half of the tile
+    const int half = ew >> 2;                // column group of the tile
     const int row = quarter * 32 + lane;     // row within the tile == TMEM lane
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    uint8_t* stage_out = s_out + ew * OUT_STAGE_BYTES_PER_WARP;
+    uint8_t* stage_out = s_out + ew * C::OUT_STAGE_BYTES_PER_WARP;
     const uint32_t stage_out_addr = smem_u32(stage_out);
 
     int acc = 0, sstage = 0;
@@ -258,26 +274,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // Software pipeline over 32-column chunks: the TMEM load of chunk c+1
         // is in flight while chunk c is promoted. Once the last chunk is in
         // registers the TMEM buffer goes back to the MMA warp, before its math.
-        uint32_t r[2][32];
-        tmem_ld_32x32b_x32(t_addr, r[0]);
+        constexpr int CH = C::CHUNK;
+        uint32_t r[2][CH];
+        tmem_ld_chunk(t_addr, r[0]);
 #pragma unroll
-        for (int c = 0; c < C::CHUNKS32; ++c) {
+        for (int c = 0; c < C::CHUNKS; ++c) {
           tmem_wait_ld_bind(r[c & 1]);
-          if (c + 1 < C::CHUNKS32) {
-            tmem_ld_32x32b_x32(t_addr + (c + 1) * 32, r[(c + 1) & 1]);
+          if (c + 1 < C::CHUNKS) {
+            tmem_ld_chunk(t_addr + (c + 1) * CH, r[(c + 1) & 1]);
           } else {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty_bar[acc]);
           }
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 sb4 = *reinterpret_cast<const float4*>(b_s + c * 32 + j);
+          for (int j = 0; j < CH; j += 4) {
+            const float4 sb4 = *reinterpret_cast<const float4*>(b_s + c * CH + j);
             const uint32_t* q = &r[c & 1][j];
             float u0, u1, u2, u3;
             mul_f32x2(u0, u1, __uint_as_float(q[0]), __uint_as_float(q[1]), sb4.x, sb4.y);
             mul_f32x2(u2, u3, __uint_as_float(q[2]), __uint_as_float(q[3]), sb4.z, sb4.w);
-            float* f = &fin[c * 32 + j];
+            float* f = &fin[c * CH + j];
             fma_f32x2(f[0], f[1], u0, u1, a_s, a_s, f[0], f[1]);
             fma_f32x2(f[2], f[3], u2, u3, a_s, a_s, f[2], f[3]);
           }
@@ -334,16 +351,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           bulk_commit_group();
         }
       } else {
-        // fp32: boxes of 32 rows x 32 columns, two boxes per staging round.
+        // fp32: boxes of 32 rows x 32 columns, PER_ROUND boxes per staging round.
         constexpr int BOXES = C::COLS_PER_WARP / 32;
+        constexpr int PER_ROUND = C::OUT_STAGE_BYTES_PER_WARP / 4096;
 #pragma unroll
-        for (int bx0 = 0; bx0 < BOXES; bx0 += 2) {
+        for (int bx0 = 0; bx0 < BOXES; bx0 += PER_ROUND) {
           if (bx0 > 0) {
             if (lane == 0) bulk_wait_group_read0();
             __syncwarp();
           }
 #pragma unroll
-          for (int bi = 0; bi < 2; ++bi) {
+          for (int bi = 0; bi < PER_ROUND; ++bi) {
             const uint32_t box = stage_out_addr + bi * 4096 + lane * 128;
 #pragma unroll
             for (int ch = 0; ch < 8; ++ch) {
@@ -356,7 +374,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           __syncwarp();
           if (lane == 0 && rows_in) {
 #pragma unroll
-            for (int bi = 0; bi < 2; ++bi) {
+            for (int bi = 0; bi < PER_ROUND; ++bi) {
               const int c = col0 + (bx0 + bi) * 32;
               if (c < p.n) tma_store_3d(&tmap_out, stage_out + bi * 4096, c, tc.m0 + quarter * 32, tc.e);
             }
@@ -379,34 +397,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 }  // namespace
 
-template <int BN>
+template <int BN, int EPI>
 static cudaError_t launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                                const GemmParams& p, int grid, cudaStream_t stream) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, EPI>;
   static int configured_device_mask = 0;  // bit per device ordinal (< 32)
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
-  if (dev < 32 && !(configured_device_mask & (1 << dev))) {
-    err = cudaFuncSetAttribute(grouped_wgrad_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (dev >= 32 || !(configured_device_mask & (1 << dev))) {
+    err = cudaFuncSetAttribute(grouped_wgrad_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                C::SMEM_BYTES);
     if (err != cudaSuccess) return err;
-    configured_device_mask |= (1 << dev);
-  } else if (dev >= 32) {
-    err = cudaFuncSetAttribute(grouped_wgrad_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               C::SMEM_BYTES);
-    if (err != cudaSuccess) return err;
+    if (dev < 32) configured_device_mask |= (1 << dev);
   }
-  grouped_wgrad_kernel<BN><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ta, tb, to, p);
+  grouped_wgrad_kernel<BN, EPI><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tb, to, p);
   return cudaGetLastError();
 }
 
 cudaError_t launch_grouped_wgrad(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                                  const GemmParams& p, int grid, cudaStream_t stream) {
-  if (p.bn == 256) return launch_impl<256>(ta, tb, to, p, grid, stream);
-  return launch_impl<128>(ta, tb, to, p, grid, stream);
+  if (p.bn == 256) {
+    return p.epi_warps == 16 ? launch_impl<256, 16>(ta, tb, to, p, grid, stream)
+                             : launch_impl<256, 8>(ta, tb, to, p, grid, stream);
+  }
+  return launch_impl<128, 8>(ta, tb, to, p, grid, stream);
 }
-
-int smem_bytes_for_bn(int bn) { return bn == 256 ? Cfg<256>::SMEM_BYTES : Cfg<128>::SMEM_BYTES; }
 
 }  // namespace wgrad

@@ -24,11 +24,11 @@ struct GemmParams {
   int out_f32;
   int accumulate;
   int has_operands;             // 0 when the operand K extent is empty
+  int epi_warps;                // promotion warps: 8, or 16 (bn 256 only)
 };
 
 cudaError_t launch_grouped_wgrad(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                                  const GemmParams& p, int grid, cudaStream_t stream);
 
-int smem_bytes_for_bn(int bn);
 
 }  // namespace wgrad

@@ -30,6 +30,8 @@ OUT_F32 = 1
 TILE_AUTO = 0
 TILE_128x256 = 1
 TILE_128x128 = 2
+TILE_128x256_W8 = 3
+TILE_128x256_W16 = 4
 
 # Every symbol include/sm100_fp8_wgrad.h declares.
 EXPORTED_SYMBOLS = (

@@ -59,6 +59,8 @@ TUNED_CONFIGS: dict[str, int] = {
     # B200-native names
     "sm100_128x256": _lib.TILE_128x256,
     "sm100_128x128": _lib.TILE_128x128,
+    "sm100_128x256_w8": _lib.TILE_128x256_W8,     # 8 promotion warps
+    "sm100_128x256_w16": _lib.TILE_128x256_W16,   # 16 promotion warps
 }
 
 

@@ -138,7 +138,7 @@ def test_quantiser_fp32_input_and_odd_columns(cuda_device):
     np.testing.assert_array_equal(op.scales.cpu().numpy().view(np.uint32), ref.scales.view(np.uint32))
 
 
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x128", "sm100_128x256"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x128", "sm100_128x256_w8", "sm100_128x256_w16"])
 @pytest.mark.parametrize("case", sorted(SMALL_CASES) + ["c1"])
 def test_grouped_wgrad_matches_oracle(cuda_device, case, tuned_config):
     from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
@@ -159,7 +159,8 @@ def test_grouped_wgrad_matches_oracle(cuda_device, case, tuned_config):
     assert _lib.device_error() == 0
 
 
-def test_grouped_wgrad_fp32_out_and_accumulate(cuda_device):
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w8", "sm100_128x256_w16"])
+def test_grouped_wgrad_fp32_out_and_accumulate(cuda_device, tuned_config):
     from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
 
     spec = SMALL_CASES["mixed"]
@@ -170,22 +171,23 @@ def test_grouped_wgrad_fp32_out_and_accumulate(cuda_device):
     m, n = ops[lk].data.shape[1], ops[rk].data.shape[1]
     ref = O.ref_scaled_wgrad(oops[lk], oops[rk], om)
     out = torch.full((e, m, n), float("nan"), device=cuda_device, dtype=torch.float32)
-    fp8_grouped_wgrad_sm90(ops[lk], ops[rk], out, meta)
+    fp8_grouped_wgrad_sm90(ops[lk], ops[rk], out, meta, tuned_config=tuned_config)
     _check_f32(out, ref)
     base = torch.randn((e, m, n), device=cuda_device, dtype=torch.float32) * float(np.abs(ref).max())
     acc = base.clone()
-    fp8_grouped_wgrad_sm90(ops[lk], ops[rk], acc, meta, accumulate=True)
+    fp8_grouped_wgrad_sm90(ops[lk], ops[rk], acc, meta, accumulate=True, tuned_config=tuned_config)
     _check_f32(acc - base, ref)
     base16 = base.to(torch.bfloat16)
     acc16 = base16.clone()
-    fp8_grouped_wgrad_sm90(ops[lk], ops[rk], acc16, meta, accumulate=True)
+    fp8_grouped_wgrad_sm90(ops[lk], ops[rk], acc16, meta, accumulate=True, tuned_config=tuned_config)
     expect = O.bf16_round(base16.float().cpu().numpy() + ref)
     got = acc16.float().cpu().numpy()
     np.testing.assert_allclose(got, expect, rtol=2 ** -7, atol=1e-5 * float(np.abs(expect).max()))
 
 
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16"])
 @pytest.mark.parametrize("hidden,inter", [(144, 80), (272, 48), (512, 128)])
-def test_grouped_wgrad_ragged_tiles(cuda_device, hidden, inter):
+def test_grouped_wgrad_ragged_tiles(cuda_device, hidden, inter, tuned_config):
     """M, N not multiples of the 128 x 256 tile; empty experts; long K."""
     from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
 
@@ -195,7 +197,7 @@ def test_grouped_wgrad_ragged_tiles(cuda_device, hidden, inter):
     for stage, (lk, rk) in STAGES.items():
         m, n = ops[lk].data.shape[1], ops[rk].data.shape[1]
         out = torch.full((6, m, n), float("nan"), device=cuda_device, dtype=torch.bfloat16)
-        fp8_grouped_wgrad_sm90(ops[lk], ops[rk], out, meta)
+        fp8_grouped_wgrad_sm90(ops[lk], ops[rk], out, meta, tuned_config=tuned_config)
         _check_bf16(out, O.ref_scaled_wgrad(oops[lk], oops[rk], om))
 
 
