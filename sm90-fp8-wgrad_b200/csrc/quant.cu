@@ -23,10 +23,11 @@
 // compact tail operands (quant.py:273-307), 32 or 64 rows: block b then
 // occupies padded rows [block_rows * b, block_rows * (b + 1)).
 //
-// HBM-bound transpose: a CTA reads a 128-row x 64-column BF16 tile with
-// 16-byte coalesced loads, reduces column amax through shared memory and
-// writes each column's 128 FP8 bytes as one contiguous 128-byte segment
-// (the operand is K-contiguous per column).
+// HBM-bound transpose: a CTA owns one scale block x a strip of 128 BF16 (64
+// fp32) columns. Every thread issues its eight 16-byte row loads before
+// writing them to shared memory; then each thread walks one column slice
+// (amax, then x / scale) and writes 16 rows at a time as one 16-byte segment
+// of the K-contiguous operand.
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -40,47 +41,32 @@ namespace wgrad {
 namespace {
 
 constexpr int QBLOCK_ROWS = 128;
-constexpr int QBLOCK_COLS = 64;
 constexpr int QTHREADS = 256;
 
+// Column strip of one CTA: 16 threads per tile row, one 16-byte vector each
+// (128 BF16 or 64 fp32 columns), eight rows-passes of 16 rows.
 template <typename T>
-__device__ __forceinline__ void load8(const T* src, float (&v)[8]);
+struct QTile {
+  static constexpr int VEC = 16 / static_cast<int>(sizeof(T));
+  static constexpr int COLS = 16 * VEC;
+  static constexpr int ROW_PASSES = QBLOCK_ROWS / (QTHREADS / 16);
+  static constexpr int PARTS = QTHREADS / COLS;               // row parts per column
+  static constexpr int ROWS_PER_PART = QBLOCK_ROWS / PARTS;   // 64 (bf16) or 32 (fp32)
+};
 
-template <>
-__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* src, float (&v)[8]) {
-  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src));
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(h[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
-
-template <>
-__device__ __forceinline__ void load8<float>(const float* src, float (&v)[8]) {
-  const float4 a = __ldg(reinterpret_cast<const float4*>(src));
-  const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
-
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f(float v) { return v; }
 template <typename T>
-__device__ __forceinline__ float load1(const T* src);
+__device__ __forceinline__ T zero_of();
 template <>
-__device__ __forceinline__ float load1<__nv_bfloat16>(const __nv_bfloat16* src) {
-  return __bfloat162float(src[0]);
-}
+__device__ __forceinline__ __nv_bfloat16 zero_of<__nv_bfloat16>() { return __float2bfloat16(0.f); }
 template <>
-__device__ __forceinline__ float load1<float>(const float* src) {
-  return src[0];
-}
+__device__ __forceinline__ float zero_of<float>() { return 0.f; }
 
-// grid: (total_blocks, ceil(cols / 64)); block: 256 threads.
+// grid: (total_blocks, ceil(cols / QTile<T>::COLS)); block: 256 threads.
 // Destination of the quantised bytes: column c's byte k of block b goes to
-// q[c * pitch + row_start[b] + k] (row_start == nullptr: 128 b, the padded
-// layout). zero_fill also writes the zero rows k >= row_count of the block.
+// q[c * pitch + row_start[b] + k] (row_start == nullptr: block_rows * b, the
+// padded layout). zero_fill also writes the zero rows k >= row_count.
 struct QuantDst {
   uint8_t* q;
   int64_t pitch;
@@ -96,86 +82,93 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
                                                                   QuantDst d0, QuantDst d1,
                                                                   float* __restrict__ scales, bool vec_ok,
                                                                   int block_rows, int64_t x_rows) {
-  __shared__ float tile[QBLOCK_ROWS][QBLOCK_COLS + 1];
-  __shared__ float s_amax[4][QBLOCK_COLS];
-  __shared__ float s_scale[QBLOCK_COLS];
+  using Q = QTile<T>;
+  // The tile keeps the input type (32 KB): row-major 16-byte writes, and the
+  // column walks below read 32 consecutive columns per warp, so neither side
+  // has shared-memory bank conflicts.
+  __shared__ __align__(16) T tile[QBLOCK_ROWS][Q::COLS];
+  __shared__ float s_amax[Q::PARTS][Q::COLS];
+  __shared__ float s_scale[Q::COLS];
 
   const int b = blockIdx.x;
-  const int64_t c0 = static_cast<int64_t>(blockIdx.y) * QBLOCK_COLS;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.y) * Q::COLS;
   const int64_t row0 = __ldg(block_row_start + b);
   const int rows = __ldg(block_row_count + b);
-  const int ncols = static_cast<int>(min(static_cast<int64_t>(QBLOCK_COLS), cols - c0));
+  const int ncols = static_cast<int>(min(static_cast<int64_t>(Q::COLS), cols - c0));
   const int tid = threadIdx.x;
 
-  // Load: 8 threads per row (8 columns each), 32 rows per pass.
+  // Load: all eight 16-byte loads of a thread are issued before any is
+  // written to shared memory, so 32 KB per CTA are in flight at once.
   {
-    const int sub = tid & 7;
-    const int r_in = tid >> 3;
-    const int cc = sub * 8;
+    const int cc = (tid & 15) * Q::VEC;
+    const int r_in = tid >> 4;
+    uint4 buf[Q::ROW_PASSES];
 #pragma unroll
-    for (int pass = 0; pass < QBLOCK_ROWS / 32; ++pass) {
-      const int r = pass * 32 + r_in;
-      float v[8];
+    for (int pass = 0; pass < Q::ROW_PASSES; ++pass) {
+      const int r = pass * 16 + r_in;
+      buf[pass] = make_uint4(0u, 0u, 0u, 0u);
       if (r < rows && cc < ncols) {
         int64_t xrow = gather_idx != nullptr ? static_cast<int64_t>(__ldg(gather_idx + row0 + r)) : row0 + r;
         if (gather_idx != nullptr && (xrow < 0 || xrow >= x_rows)) {
           // Out-of-range gather index: read nothing, flag the device error word.
           record_device_error(kDevBadGatherIndex);
-          xrow = -1;
+          continue;  // zeros
         }
-        const T* src = x + (xrow < 0 ? 0 : xrow) * cols + c0 + cc;
-        if (xrow < 0) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = 0.f;
-        } else if (vec_ok && cc + 8 <= ncols) {
-          load8<T>(src, v);
+        const T* src = x + xrow * cols + c0 + cc;
+        if (vec_ok && cc + Q::VEC <= ncols) {
+          buf[pass] = __ldg(reinterpret_cast<const uint4*>(src));
         } else {
+          T v[Q::VEC];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = (cc + i < ncols) ? load1<T>(src + i) : 0.f;
+          for (int i = 0; i < Q::VEC; ++i) v[i] = (cc + i < ncols) ? src[i] : zero_of<T>();
+          buf[pass] = *reinterpret_cast<const uint4*>(v);
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.f;
       }
+    }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) tile[r][cc + i] = v[i];
+    for (int pass = 0; pass < Q::ROW_PASSES; ++pass) {
+      *reinterpret_cast<uint4*>(&tile[pass * 16 + r_in][cc]) = buf[pass];
     }
   }
   __syncthreads();
 
-  // Column amax: 4 threads per column, 32 rows each.
+  // Column amax: thread (col, part) walks ROWS_PER_PART rows of one column.
+  const int col = tid % Q::COLS;
+  const int part = tid / Q::COLS;
+  const int k_begin = part * Q::ROWS_PER_PART;
   {
-    const int col = tid & 63;
-    const int part = tid >> 6;
     float m = 0.f;
-#pragma unroll 8
-    for (int r = part * 32; r < part * 32 + 32; ++r) m = fmaxf(m, fabsf(tile[r][col]));
+#pragma unroll 16
+    for (int k = k_begin; k < k_begin + Q::ROWS_PER_PART; ++k) m = fmaxf(m, fabsf(to_f(tile[k][col])));
     s_amax[part][col] = m;
   }
   __syncthreads();
-  if (tid < QBLOCK_COLS) {
-    const float amax = fmaxf(fmaxf(s_amax[0][tid], s_amax[1][tid]), fmaxf(s_amax[2][tid], s_amax[3][tid]));
+  if (tid < Q::COLS) {
+    float amax = s_amax[0][tid];
+#pragma unroll
+    for (int pp = 1; pp < Q::PARTS; ++pp) amax = fmaxf(amax, s_amax[pp][tid]);
     const float scale = fmaxf(__fdiv_rn(amax, 448.0f), 1.0e-12f);
     s_scale[tid] = scale;
     if (tid < ncols) scales[static_cast<int64_t>(b) * cols + c0 + tid] = scale;
   }
   __syncthreads();
+  if (col >= ncols) return;
 
-  // Store: each 16-row chunk of column c's bytes as one 16-byte vector when the
-  // destination is aligned and the chunk is entirely written, else bytewise.
-  for (int idx = tid; idx < QBLOCK_COLS * 8; idx += QTHREADS) {
-    const int col = idx >> 3;
-    const int chunk = idx & 7;
-    if (col >= ncols) continue;
-    const float s = s_scale[col];
+  // Quantise the same column slice: 16 rows -> one 16-byte segment of the
+  // K-contiguous operand, vector-stored when aligned and entirely written.
+  const float s = s_scale[col];
+#pragma unroll
+  for (int ch = 0; ch < Q::ROWS_PER_PART / 16; ++ch) {
+    const int k0 = k_begin + ch * 16;
+    if (k0 >= block_rows) break;
     uint32_t w[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int k = chunk * 16 + i * 4;
-      const float f0 = __fdiv_rn(tile[k + 0][col], s);
-      const float f1 = __fdiv_rn(tile[k + 1][col], s);
-      const float f2 = __fdiv_rn(tile[k + 2][col], s);
-      const float f3 = __fdiv_rn(tile[k + 3][col], s);
+      const int k = k0 + i * 4;
+      const float f0 = __fdiv_rn(to_f(tile[k + 0][col]), s);
+      const float f1 = __fdiv_rn(to_f(tile[k + 1][col]), s);
+      const float f2 = __fdiv_rn(to_f(tile[k + 2][col]), s);
+      const float f3 = __fdiv_rn(to_f(tile[k + 3][col]), s);
       const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(f0, f1), __NV_SATFINITE, __NV_E4M3);
       const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(f2, f3), __NV_SATFINITE, __NV_E4M3);
       w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
@@ -184,15 +177,15 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
     for (int o = 0; o < 2; ++o) {
       const QuantDst& d = o == 0 ? d0 : d1;
       if (d.q == nullptr) continue;
+      const int limit = d.zero_fill ? block_rows : rows;  // rows k < limit are written
+      if (k0 >= limit) continue;
       const int64_t start = d.row_start != nullptr ? static_cast<int64_t>(__ldg(d.row_start + b))
                                                    : static_cast<int64_t>(b) * block_rows;
-      const int limit = d.zero_fill ? block_rows : rows;  // rows k < limit are written
-      if (chunk * 16 >= limit) continue;
-      uint8_t* dst = d.q + (c0 + col) * d.pitch + start + chunk * 16;
-      if (chunk * 16 + 16 <= limit && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+      uint8_t* dst = d.q + (c0 + col) * d.pitch + start + k0;
+      if (k0 + 16 <= limit && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
         *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
       } else {
-        for (int i = 0; i < 16 && chunk * 16 + i < limit; ++i) dst[i] = static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3)));
+        for (int i = 0; i < 16 && k0 + i < limit; ++i) dst[i] = static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3)));
       }
     }
   }
@@ -206,7 +199,8 @@ cudaError_t launch_quantize_1x128(const void* x, int x_dtype, int64_t cols, cons
                                   bool q_zero_fill, void* kq, int64_t kq_pitch, const int32_t* kq_row_start,
                                   float* scales, int block_rows, int64_t x_rows, cudaStream_t stream) {
   if (total_blocks == 0 || cols == 0) return cudaSuccess;
-  const dim3 grid(static_cast<unsigned>(total_blocks), static_cast<unsigned>((cols + QBLOCK_COLS - 1) / QBLOCK_COLS));
+  const int strip = x_dtype == 0 ? QTile<__nv_bfloat16>::COLS : QTile<float>::COLS;
+  const dim3 grid(static_cast<unsigned>(total_blocks), static_cast<unsigned>((cols + strip - 1) / strip));
   const QuantDst d0{static_cast<uint8_t*>(q), q_pitch, q_row_start, q_zero_fill};
   const QuantDst d1{static_cast<uint8_t*>(kq), kq_pitch, kq_row_start, false};
   if (x_dtype == 0) {
