@@ -405,19 +405,28 @@ def run_ours(args) -> None:
 def run_e2e(inp, args, world, dev, step_flops) -> dict:
     """Same metric through the public API with host buffers: every step copies
     its inputs (FP8 operands, scales, metadata) from pinned host memory to the
-    device, runs both GEMMs and copies both gradients back to pinned host memory."""
-    from sm90_fp8_wgrad.synthetic import run_custom_down, run_custom_gate_up
+    device, runs both GEMMs and copies both gradients back to pinned host memory.
 
-    dev_inputs = []
-    for op in (inp.grad_y_q, inp.hidden_q, inp.grad_gate_up_q, inp.x_q):
+    The step is pipelined over three streams, as a caller of the operator would
+    run it: the inputs go host-to-device on one copy stream (the down GEMM's
+    first, so it can start early); the GEMMs run on the compute stream in
+    expert chunks (``expert_range`` launches, bit-identical to one launch); and
+    each finished chunk of gradients goes device-to-host on a second copy stream
+    while the next chunks compute. Consecutive steps only wait where they reuse
+    a buffer (next inputs after this step's GEMMs, a chunk's output after its
+    previous copy-out)."""
+    from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
+
+    def storage_of(op):
         if op.kernel_data is not None:        # packed layout: the launch copy is what the GEMM reads
-            storage = op.kernel_data
-        else:
-            pitch = op.data.stride(1)
-            storage = op.data.as_strided((op.data.shape[1], pitch), (pitch, 1))
-        dev_inputs += [storage, op.scales]
+            return op.kernel_data
+        pitch = op.data.stride(1)
+        return op.data.as_strided((op.data.shape[1], pitch), (pitch, 1))
+
     m = inp.meta
-    dev_inputs += [m.padded_cu_seqlens_k, m.wgmma_cu_seqlens_k, m.block_offsets, m.expert_order]
+    meta_in = [m.padded_cu_seqlens_k, m.wgmma_cu_seqlens_k, m.block_offsets, m.expert_order]
+    down_in = [storage_of(inp.grad_y_q), inp.grad_y_q.scales, storage_of(inp.hidden_q), inp.hidden_q.scales]
+    gate_in = [storage_of(inp.grad_gate_up_q), inp.grad_gate_up_q.scales, storage_of(inp.x_q), inp.x_q.scales]
     outs = [inp.down_out_bf16, inp.gate_up_out_bf16]
 
     def pinned_like(t):
@@ -426,37 +435,69 @@ def run_e2e(inp, args, world, dev, step_flops) -> dict:
         except RuntimeError:
             return torch.empty(t.shape, dtype=t.dtype)
 
-    host_in = [pinned_like(t) for t in dev_inputs]
-    for h_t, d_t in zip(host_in, dev_inputs):
-        h_t.copy_(d_t)
+    groups = [meta_in + down_in, gate_in]
+    host_in = [[pinned_like(t) for t in g] for g in groups]
+    for hg, dg in zip(host_in, groups):
+        for h_t, d_t in zip(hg, dg):
+            h_t.copy_(d_t)
     host_out = [pinned_like(t) for t in outs]
-    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    h2d = sum(t.numel() * t.element_size() for g in host_in for t in g)
     d2h = sum(t.numel() * t.element_size() for t in host_out)
     steps = max(1, min(args.steps, args.e2e_steps))
 
+    experts = inp.experts
+    n_chunks = max(1, min(16, experts))
+    bounds = [experts * c // n_chunks for c in range(n_chunks + 1)]
+    chunks = [(a, b) for a, b in zip(bounds[:-1], bounds[1:]) if b > a]
+    s_h2d, s_cmp, s_d2h = (torch.cuda.Stream(dev) for _ in range(3))
+    ev_in = [torch.cuda.Event() for _ in groups]
+    ev_cmp = [[torch.cuda.Event() for _ in chunks] for _ in outs]
+    ev_out = [[torch.cuda.Event() for _ in chunks] for _ in outs]
+    ev_gemms_done = torch.cuda.Event()
+    gemms = [(inp.grad_y_q, inp.hidden_q), (inp.grad_gate_up_q, inp.x_q)]
+
     def step():
-        for h_t, d_t in zip(host_in, dev_inputs):
-            d_t.copy_(h_t, non_blocking=True)
-        run_custom_down(inp)
-        run_custom_gate_up(inp)
-        for h_t, d_t in zip(host_out, outs):
-            h_t.copy_(d_t, non_blocking=True)
+        s_h2d.wait_event(ev_gemms_done)               # the previous step's GEMMs are done reading
+        with torch.cuda.stream(s_h2d):
+            for g, (hg, dg) in enumerate(zip(host_in, groups)):
+                for h_t, d_t in zip(hg, dg):
+                    d_t.copy_(h_t, non_blocking=True)
+                ev_in[g].record(s_h2d)
+        for g, ((lhs, rhs), out) in enumerate(zip(gemms, outs)):
+            s_cmp.wait_event(ev_in[g])
+            for c, (e0, e1) in enumerate(chunks):
+                s_cmp.wait_event(ev_out[g][c])         # the previous copy-out of this chunk is done
+                with torch.cuda.stream(s_cmp):
+                    fp8_grouped_wgrad_sm90(lhs, rhs, out, m, expert_range=(e0, e1))
+                ev_cmp[g][c].record(s_cmp)
+                s_d2h.wait_event(ev_cmp[g][c])
+                with torch.cuda.stream(s_d2h):
+                    host_out[g][e0:e1].copy_(out[e0:e1], non_blocking=True)
+                ev_out[g][c].record(s_d2h)
+        ev_gemms_done.record(s_cmp)
 
     step()
+    torch.cuda.synchronize(dev)
     _barrier(world, dev)
     stream = torch.cuda.current_stream(dev)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
+    for s_ in (s_h2d, s_cmp, s_d2h):
+        s_.wait_event(t0)
     for _ in range(steps):
         step()
+    for s_ in (s_h2d, s_cmp, s_d2h):
+        e_ = torch.cuda.Event()
+        e_.record(s_)
+        stream.wait_event(e_)
     t1.record(stream)
     torch.cuda.synchronize(dev)
     ms = _max_over_ranks(t0.elapsed_time(t1) / steps, world, dev)
     flops = _sum_over_ranks(step_flops, world, dev)
     return {"value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
-            "pinned": bool(host_in[0].is_pinned())}
+            "pinned": bool(host_in[0][0].is_pinned()), "chunks": len(chunks), "streams": 3}
 
 
 def main() -> None:

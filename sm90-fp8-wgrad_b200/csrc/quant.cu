@@ -63,6 +63,26 @@ __device__ __forceinline__ __nv_bfloat16 zero_of<__nv_bfloat16>() { return __flo
 template <>
 __device__ __forceinline__ float zero_of<float>() { return 0.f; }
 
+constexpr int QSTAGE_PITCH = 144;  // bytes per staged FP8 column (128 + 16 pad)
+
+// x / s rounded to nearest even, for the quantiser's positive scale s, from the
+// correctly rounded reciprocal rs = RN(1/s) and one FMA correction step
+// (Markstein's theorem, IBM J. Res. Dev. 34(1), 1990; also Muller et al.,
+// Handbook of Floating-Point Arithmetic, sec. 4.7): q0 = RN(x rs) is faithful,
+// the remainder x - s q0 is exact in one FMA, and RN(q0 + rem rs) is the
+// correctly rounded quotient when nothing overflows or underflows. Quotients
+// small enough for the remainder to underflow are far below the smallest e4m3
+// subnormal (they encode as zero either way). The sign of a zero quotient is
+// taken from x, as IEEE division gives it; an infinite scale uses the
+// division directly.
+__device__ __forceinline__ float div_rn_by_scale(float x, float s, float rs, bool finite_scale) {
+  if (!finite_scale) return __fdiv_rn(x, s);
+  const float q0 = x * rs;
+  const float rem = fmaf(-q0, s, x);
+  const float q1 = fmaf(rem, rs, q0);
+  return __int_as_float(__float_as_int(q1) | (__float_as_int(x) & static_cast<int>(0x80000000u)));
+}
+
 // grid: (total_blocks, ceil(cols / QTile<T>::COLS)); block: 256 threads.
 // Destination of the quantised bytes: column c's byte k of block b goes to
 // q[c * pitch + row_start[b] + k] (row_start == nullptr: block_rows * b, the
@@ -152,27 +172,46 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
     if (tid < ncols) scales[static_cast<int64_t>(b) * cols + c0 + tid] = scale;
   }
   __syncthreads();
-  if (col >= ncols) return;
-
-  // Quantise the same column slice: 16 rows -> one 16-byte segment of the
-  // K-contiguous operand, vector-stored when aligned and entirely written.
-  const float s = s_scale[col];
+  // Quantise the column slice into registers: 16 rows -> one 16-byte word.
+  constexpr int CH = Q::ROWS_PER_PART / 16;
+  uint4 qv[CH];
+  if (col < ncols) {
+    const float s = s_scale[col];
+    const float rs = __frcp_rn(s);
+    const bool finite_scale = isfinite(s);
 #pragma unroll
-  for (int ch = 0; ch < Q::ROWS_PER_PART / 16; ++ch) {
-    const int k0 = k_begin + ch * 16;
-    if (k0 >= block_rows) break;
-    uint32_t w[4];
+    for (int ch = 0; ch < CH; ++ch) {
+      uint32_t w[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int k = k0 + i * 4;
-      const float f0 = __fdiv_rn(to_f(tile[k + 0][col]), s);
-      const float f1 = __fdiv_rn(to_f(tile[k + 1][col]), s);
-      const float f2 = __fdiv_rn(to_f(tile[k + 2][col]), s);
-      const float f3 = __fdiv_rn(to_f(tile[k + 3][col]), s);
-      const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(f0, f1), __NV_SATFINITE, __NV_E4M3);
-      const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(f2, f3), __NV_SATFINITE, __NV_E4M3);
-      w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+      for (int i = 0; i < 4; ++i) {
+        const int k = k_begin + ch * 16 + i * 4;
+        float f[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f[j] = div_rn_by_scale(to_f(tile[k + j][col]), s, rs, finite_scale);
+        const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(f[0], f[1]), __NV_SATFINITE, __NV_E4M3);
+        const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(f[2], f[3]), __NV_SATFINITE, __NV_E4M3);
+        w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+      }
+      qv[ch] = make_uint4(w[0], w[1], w[2], w[3]);
     }
+  }
+  __syncthreads();  // the input tile is no longer read: reuse it as FP8 staging
+
+  // Stage column-major (column c's 128 bytes at c * QSTAGE_PITCH; the 16-byte
+  // pad spreads the 16-byte stores of consecutive columns over all banks),
+  // then write each column's bytes as full 128-byte lines, 8 threads a line.
+  uint8_t* stage = reinterpret_cast<uint8_t*>(&tile[0][0]);
+  if (col < ncols) {
+#pragma unroll
+    for (int ch = 0; ch < CH; ++ch)
+      *reinterpret_cast<uint4*>(stage + col * QSTAGE_PITCH + k_begin + ch * 16) = qv[ch];
+  }
+  __syncthreads();
+  for (int idx = tid; idx < ncols * 8; idx += QTHREADS) {
+    const int c = idx >> 3;
+    const int k0 = (idx & 7) * 16;
+    if (k0 >= block_rows) continue;
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + c * QSTAGE_PITCH + k0);
 #pragma unroll
     for (int o = 0; o < 2; ++o) {
       const QuantDst& d = o == 0 ? d0 : d1;
@@ -181,10 +220,11 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
       if (k0 >= limit) continue;
       const int64_t start = d.row_start != nullptr ? static_cast<int64_t>(__ldg(d.row_start + b))
                                                    : static_cast<int64_t>(b) * block_rows;
-      uint8_t* dst = d.q + (c0 + col) * d.pitch + start + k0;
+      uint8_t* dst = d.q + (c0 + c) * d.pitch + start + k0;
       if (k0 + 16 <= limit && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
-        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(dst) = v;
       } else {
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         for (int i = 0; i < 16 && k0 + i < limit; ++i) dst[i] = static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3)));
       }
     }

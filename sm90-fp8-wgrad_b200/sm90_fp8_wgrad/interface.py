@@ -119,6 +119,7 @@ def fp8_grouped_wgrad_sm90(
     output_layout: Literal["emn"] = "emn",
     tuned_config: str = "default",
     accumulate: bool = False,
+    expert_range: tuple[int, int] | None = None,
 ) -> torch.Tensor:
     """Grouped scaled FP8 Wgrad (runs the sm_100a engine; name kept for drop-in).
 
@@ -132,6 +133,12 @@ def fp8_grouped_wgrad_sm90(
 
     with b over expert e's 128-row scale blocks; experts without rows give 0.
     Runs on the current CUDA stream of ``out``'s device; returns ``out``.
+
+    ``expert_range=(e0, e1)`` (B200 addition, keyword only) computes only
+    out[e0:e1] and leaves the other experts untouched: one launch over that
+    expert range of the same operands and metadata, bit-identical to the
+    corresponding slice of a full launch. It lets a caller overlap the
+    device-to-host copy of finished experts with the rest of the GEMM.
     """
     layout_mode = resolve_wgrad_layout_mode()
     _check_fp8_operand("lhs", lhs)
@@ -231,6 +238,18 @@ def fp8_grouped_wgrad_sm90(
     args.block_offsets = meta.block_offsets.data_ptr()
     args.k_row_offsets = k_row_offsets.data_ptr()
     args.expert_order = order.data_ptr() if order is not None and experts > 0 else None
+    if expert_range is not None:
+        e0, e1 = (int(v) for v in expert_range)
+        if not 0 <= e0 <= e1 <= experts:
+            raise RuntimeError(f"expert_range {expert_range!r} outside [0, {experts}]")
+        # The kernel reads block_offsets[e] / k_row_offsets[e] (absolute block
+        # and row indices), so a sub-range is a pointer offset of those arrays
+        # and of out; the expert order falls back to natural order.
+        args.num_experts = e1 - e0
+        args.out = out.data_ptr() + e0 * m * n * out.element_size()
+        args.block_offsets = meta.block_offsets.data_ptr() + 4 * e0
+        args.k_row_offsets = k_row_offsets.data_ptr() + 4 * e0
+        args.expert_order = None
     args.tile_config = TUNED_CONFIGS[resolved]
     args.max_ctas = int(os.environ.get("SM100_WGRAD_MAX_CTAS", "0") or 0)
     lib = _lib.load()

@@ -216,3 +216,25 @@ def test_interface_validation_errors(cuda_device):
         fp8_grouped_wgrad_sm90(lhs, rhs, out, meta, tuned_config="nope")
     with pytest.raises(RuntimeError, match="contiguous"):
         fp8_grouped_wgrad_sm90(lhs, rhs, out.transpose(1, 2), meta)
+
+
+@pytest.mark.parametrize("splits", [[0, 2, 5, 8], [0, 0, 3, 3, 8], [0, 8]])
+def test_expert_range_launches_equal_full_launch(cuda_device, splits):
+    """out[e0:e1] from expert-range launches equals the full launch bit for bit
+    (experts are independent); the experts outside a range stay untouched."""
+    from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
+
+    spec = C1
+    meta, _, ops = _gpu_case(spec, cuda_device)
+    e = len(spec["counts"])
+    for lk, rk in STAGES.values():
+        m, n = ops[lk].data.shape[1], ops[rk].data.shape[1]
+        full = torch.empty((e, m, n), device=cuda_device, dtype=torch.bfloat16)
+        fp8_grouped_wgrad_sm90(ops[lk], ops[rk], full, meta)
+        part = torch.full((e, m, n), float("nan"), device=cuda_device, dtype=torch.bfloat16)
+        for a, b in zip(splits[:-1], splits[1:]):
+            fp8_grouped_wgrad_sm90(ops[lk], ops[rk], part, meta, expert_range=(a, b))
+            assert torch.isnan(part[b:].float()).all() or b == e
+        assert torch.equal(part.view(torch.int16), full.view(torch.int16))
+    with pytest.raises(RuntimeError, match="expert_range"):
+        fp8_grouped_wgrad_sm90(ops[lk], ops[rk], full, meta, expert_range=(3, 2))
