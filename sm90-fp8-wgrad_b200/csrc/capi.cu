@@ -6,6 +6,8 @@
 #include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "../../include/sm100_fp8_wgrad.h"
@@ -211,6 +213,9 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   p.accumulate = a->accumulate != 0;
   p.has_operands = has_operands ? 1 : 0;
   p.epi_warps = pick_epi_warps(a->tile_config, bn, a->total_blocks, a->num_experts);
+  // Test-only failure injection of the bounded-wait path (never set in normal use).
+  const char* inject = std::getenv("SM100_WGRAD_DEBUG_INJECT");
+  p.inject = (inject != nullptr && std::strcmp(inject, "withhold_first_load") == 0) ? wgrad::kInjectWithholdFirstLoad : 0;
 
   int grid = info.sm_count;
   if (a->max_ctas > 0 && a->max_ctas < grid) grid = a->max_ctas;

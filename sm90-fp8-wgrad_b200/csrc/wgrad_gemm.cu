@@ -184,8 +184,13 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
           ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, kDevTimeoutProducer);
           if (!ok) break;
           mbar_arrive_expect_tx(&full_bar[stage], C::A_BYTES + C::B_BYTES);
-          tma_load_2d(s_a + stage * C::A_BYTES, &tmap_a, &full_bar[stage], krow0 + kb * BK, tc.m0);
-          tma_load_2d(s_b + stage * C::B_BYTES, &tmap_b, &full_bar[stage], krow0 + kb * BK, tc.n0);
+          // Test-only failure injection: announce the first stage's bytes but
+          // issue no copy, so the stage never fills and the bounded waits of
+          // the consumers expire (device error word, clean exit).
+          if (!(p.inject == kInjectWithholdFirstLoad && tile == static_cast<int>(blockIdx.x) && kb == 0)) {
+            tma_load_2d(s_a + stage * C::A_BYTES, &tmap_a, &full_bar[stage], krow0 + kb * BK, tc.m0);
+            tma_load_2d(s_b + stage * C::B_BYTES, &tmap_b, &full_bar[stage], krow0 + kb * BK, tc.n0);
+          }
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
 
           ok = mbar_wait(&sempty_bar[sstage], sphase ^ 1u, abort_flag, kDevTimeoutProducer);

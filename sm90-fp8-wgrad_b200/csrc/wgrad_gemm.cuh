@@ -8,6 +8,10 @@
 
 namespace wgrad {
 
+// Test-only failure injection (SM100_WGRAD_DEBUG_INJECT=withhold_first_load):
+// the producer announces its first stage's bytes without issuing the copy.
+constexpr int kInjectWithholdFirstLoad = 1;
+
 struct GemmParams {
   const float* sa;              // lhs scales [total_blocks][m]
   const float* sb;              // rhs scales [total_blocks][n]
@@ -25,6 +29,7 @@ struct GemmParams {
   int accumulate;
   int has_operands;             // 0 when the operand K extent is empty
   int epi_warps;                // promotion warps: 8, or 16 (bn 256 only)
+  int inject;                   // test-only failure injection (kInject*), 0 in normal use
 };
 
 cudaError_t launch_grouped_wgrad(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
