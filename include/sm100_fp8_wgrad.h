@@ -195,6 +195,14 @@ SM100_WGRAD_API int sm100_wgrad_build_meta(const int32_t* cu_seqlens_k, int64_t 
  * index outside [0, x_rows). The first error since the last read is kept. */
 SM100_WGRAD_API int sm100_wgrad_device_error(int32_t* code);
 
+/* Per-role cycle counters of the grouped GEMM, summed over CTAs since the last
+ * read (synchronous; reads and clears). Only a library built with
+ * -DWGRAD_PROFILE=1 (build_ext.py --profile) records them; the product build
+ * returns SM100_WGRAD_ERR_UNSUPPORTED. Slots 0-10: producer wait for a stage,
+ * producer wait for a scale stage, MMA wait, MMA issue, promotion wait,
+ * promotion, tile store, wait for the previous store, K blocks, tiles, CTAs. */
+SM100_WGRAD_API int sm100_wgrad_profile_counters(uint64_t* counters, int32_t n);
+
 /* Human-readable text of a status code (static storage). */
 SM100_WGRAD_API const char* sm100_wgrad_status_string(int status);
 

@@ -1,7 +1,10 @@
 """Build libsm100_fp8_wgrad.so (sm_100a) in-tree with nvcc.
 
-Usage: python sm90-fp8-wgrad_b200/build_ext.py [--force]
+Usage: python sm90-fp8-wgrad_b200/build_ext.py [--force] [--profile]
 Output: sm90-fp8-wgrad_b200/sm90_fp8_wgrad/_lib/libsm100_fp8_wgrad.so
+        (--profile: libsm100_fp8_wgrad_profile.so, the same library with the
+        GEMM's per-role cycle counters compiled in, -DWGRAD_PROFILE=1; load it
+        with SM100_WGRAD_LIB=<path> and read sm90_fp8_wgrad._lib.profile_counters())
 """
 from __future__ import annotations
 
@@ -15,6 +18,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 OUT = HERE / "sm90_fp8_wgrad" / "_lib" / "libsm100_fp8_wgrad.so"
+OUT_PROFILE = HERE / "sm90_fp8_wgrad" / "_lib" / "libsm100_fp8_wgrad_profile.so"
 SOURCES = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [HERE.parent / "include" / "sm100_fp8_wgrad.h"]
 
 
@@ -25,21 +29,23 @@ def nvcc_path() -> str:
     raise RuntimeError("nvcc not found")
 
 
-def needs_build() -> bool:
-    if not OUT.exists():
+def needs_build(out: Path = OUT) -> bool:
+    if not out.exists():
         return True
-    mtime = OUT.stat().st_mtime
+    mtime = out.stat().st_mtime
     return any(s.stat().st_mtime > mtime for s in SOURCES)
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and not needs_build():
-        return OUT
-    OUT.parent.mkdir(parents=True, exist_ok=True)
-    tmp = OUT.with_suffix(".so.tmp")
+def build(force: bool = False, verbose: bool = False, profile: bool = False) -> Path:
+    out = OUT_PROFILE if profile else OUT
+    if not force and not needs_build(out):
+        return out
+    out.parent.mkdir(parents=True, exist_ok=True)
+    tmp = out.with_suffix(".so.tmp")
     cmd = [
         nvcc_path(), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
         "-shared", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-Xptxas", "-v" if verbose else "-O3",
+        *(["-DWGRAD_PROFILE=1"] if profile else []),
         "-o", str(tmp), str(CSRC / "unity.cu"),
     ]
     res = subprocess.run(cmd, capture_output=True, text=True)
@@ -47,13 +53,14 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     if verbose:
         sys.stderr.write(res.stderr)
-    os.replace(tmp, OUT)
-    return OUT
+    os.replace(tmp, out)
+    return out
 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="build the per-role cycle-counter library")
     a = ap.parse_args()
-    print(build(force=a.force, verbose=a.verbose))
+    print(build(force=a.force, verbose=a.verbose, profile=a.profile))

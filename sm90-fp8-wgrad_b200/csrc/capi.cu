@@ -289,6 +289,20 @@ int sm100_wgrad_build_meta(const int32_t* cu_seqlens_k, int64_t num_experts, con
   return err == cudaSuccess ? SM100_WGRAD_OK : SM100_WGRAD_ERR_LAUNCH;
 }
 
+int sm100_wgrad_profile_counters(uint64_t* counters, int32_t n) {
+  if (counters == nullptr || n < 0) return SM100_WGRAD_ERR_INVALID_ARG;
+#if WGRAD_PROFILE
+  unsigned long long v[wgrad::kProfSlots] = {0};
+  if (cudaMemcpyFromSymbol(v, wgrad::g_wgrad_prof, sizeof(v)) != cudaSuccess) return SM100_WGRAD_ERR_LAUNCH;
+  const unsigned long long z[wgrad::kProfSlots] = {0};
+  if (cudaMemcpyToSymbol(wgrad::g_wgrad_prof, z, sizeof(z)) != cudaSuccess) return SM100_WGRAD_ERR_LAUNCH;
+  for (int i = 0; i < n && i < wgrad::kProfSlots; ++i) counters[i] = v[i];
+  return SM100_WGRAD_OK;
+#else
+  return SM100_WGRAD_ERR_UNSUPPORTED;  // library built without WGRAD_PROFILE
+#endif
+}
+
 int sm100_wgrad_device_error(int32_t* code) {
   if (code == nullptr) return SM100_WGRAD_ERR_INVALID_ARG;
   unsigned int v = 0, zero = 0;

@@ -44,6 +44,28 @@
 
 namespace wgrad {
 
+// Per-role cycle counters (build with -DWGRAD_PROFILE=1; read and cleared by
+// sm100_wgrad_profile_counters). One lane of the producer, the MMA warp and
+// the first promotion warp of every CTA times its waits and work with clock64;
+// the CTA's sums go to g_wgrad_prof at exit. Slots: see kProf* in
+// wgrad_gemm.cuh. Off by default: the product build has no timing code.
+#if WGRAD_PROFILE
+__device__ unsigned long long g_wgrad_prof[kProfSlots];
+#define WGRAD_PROF_T(v) const long long v = clock64()
+#define WGRAD_PROF_ADD(slot, t0) \
+  do {                           \
+    if (prof_lane) s_prof[slot] += static_cast<unsigned long long>(clock64() - (t0)); \
+  } while (0)
+#define WGRAD_PROF_INC(slot) \
+  do {                       \
+    if (prof_lane) s_prof[slot] += 1ull; \
+  } while (0)
+#else
+#define WGRAD_PROF_T(v) ((void)0)
+#define WGRAD_PROF_ADD(slot, t0) ((void)0)
+#define WGRAD_PROF_INC(slot) ((void)0)
+#endif
+
 namespace {
 
 constexpr int BM = 128;
@@ -134,6 +156,11 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+#if WGRAD_PROFILE
+  __shared__ unsigned long long s_prof[kProfSlots];
+  const bool prof_lane = lane == 0 && (warp == 0 || warp == 1 || warp == FIRST_EPI_WARP);
+  if (threadIdx.x < kProfSlots) s_prof[threadIdx.x] = threadIdx.x == kProfCtas ? 1ull : 0ull;
+#endif
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -181,7 +208,9 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
         const uint32_t b_scale_bytes = static_cast<uint32_t>(min(BN, p.n - tc.n0)) * 4u;
         bool ok = true;
         for (int kb = 0; kb < nkb && ok; ++kb) {
+          WGRAD_PROF_T(tw0);
           ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, kDevTimeoutProducer);
+          WGRAD_PROF_ADD(kProfProducerWaitStage, tw0);
           if (!ok) break;
           mbar_arrive_expect_tx(&full_bar[stage], C::A_BYTES + C::B_BYTES);
           // Test-only failure injection: announce the first stage's bytes but
@@ -193,7 +222,9 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
 
+          WGRAD_PROF_T(tw1);
           ok = mbar_wait(&sempty_bar[sstage], sphase ^ 1u, abort_flag, kDevTimeoutProducer);
+          WGRAD_PROF_ADD(kProfProducerWaitScales, tw1);
           if (!ok) break;
           float* dst = s_scale + sstage * C::SCALE_FLOATS;
           const size_t blk = static_cast<size_t>(kb0 + kb);
@@ -222,7 +253,10 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
       for (int kb = 0; kb < nkb; ++kb) {
         const int atoms = kb + 1 == nkb ? last_atoms : BK / 32;
         // Whole warp waits (keeps the warp converged for the .sync.aligned ops).
+        WGRAD_PROF_T(tm0);
         ok = mbar_wait2(&tempty_bar[acc], aphase ^ 1u, &full_bar[stage], phase, abort_flag, kDevTimeoutMma);
+        WGRAD_PROF_ADD(kProfMmaWait, tm0);
+        WGRAD_PROF_T(tm1);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
@@ -241,6 +275,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
           umma_commit(&tfull_bar[acc]);
         }
         __syncwarp();
+        WGRAD_PROF_ADD(kProfMmaIssue, tm1);
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         acc ^= 1;
         if (acc == 0) aphase ^= 1u;
@@ -268,7 +303,10 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
       for (int j = 0; j < C::COLS_PER_WARP; ++j) fin[j] = 0.f;
 
       for (int kb = 0; kb < nkb; ++kb) {
+        WGRAD_PROF_T(te0);
         ok = mbar_wait2(&tfull_bar[acc], aphase, &sfull_bar[sstage], sphase, abort_flag, kDevTimeoutEpilogue);
+        WGRAD_PROF_ADD(kProfEpiWait, te0);
+        WGRAD_PROF_T(te1);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
@@ -306,6 +344,8 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sempty_bar[sstage]);
+        WGRAD_PROF_ADD(kProfEpiPromote, te1);
+        WGRAD_PROF_INC(kProfKBlocks);
         acc ^= 1;
         if (acc == 0) aphase ^= 1u;
         if (++sstage == SCALE_STAGES) { sstage = 0; sphase ^= 1u; }
@@ -313,6 +353,8 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
       if (!ok) break;
 
       // -------------------------------------------------------- epilogue store
+      WGRAD_PROF_T(ts0);
+      WGRAD_PROF_INC(kProfTiles);
       const int g_row = tc.m0 + row;
       const int col0 = tc.n0 + half * C::COLS_PER_WARP;
       if (p.accumulate) {
@@ -328,8 +370,10 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
         }
       }
       // The previous tile's TMA store must have finished reading the staging buffer.
+      WGRAD_PROF_T(ts1);
       if (lane == 0) bulk_wait_group_read0();
       __syncwarp();
+      WGRAD_PROF_ADD(kProfEpiStoreWait, ts1);
       const bool rows_in = (tc.m0 + quarter * 32) < p.m;
       const uint32_t swz = static_cast<uint32_t>(lane & 7);
       if (!p.out_f32) {
@@ -387,6 +431,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
           }
         }
       }
+      WGRAD_PROF_ADD(kProfEpiStore, ts0);
     }
     if (lane == 0) bulk_wait_group0();  // all output writes complete before exit
     __syncwarp();
@@ -394,6 +439,9 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+#if WGRAD_PROFILE
+  if (threadIdx.x < kProfSlots) atomicAdd(&g_wgrad_prof[threadIdx.x], s_prof[threadIdx.x]);
+#endif
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);

@@ -8,6 +8,26 @@
 
 namespace wgrad {
 
+#ifndef WGRAD_PROFILE
+#define WGRAD_PROFILE 0
+#endif
+
+// Slots of the per-role cycle counters (WGRAD_PROFILE builds), summed over CTAs.
+enum ProfSlot : int {
+  kProfProducerWaitStage = 0,   // producer: waits for a free operand stage
+  kProfProducerWaitScales = 1,  // producer: waits for a free scale stage
+  kProfMmaWait = 2,             // MMA warp: waits for a free TMEM buffer + a full stage
+  kProfMmaIssue = 3,            // MMA warp: issuing the K block's UMMAs and commits
+  kProfEpiWait = 4,             // promotion warp: waits for the partial + scales
+  kProfEpiPromote = 5,          // promotion warp: TMEM loads + fp32 promotion of a K block
+  kProfEpiStore = 6,            // promotion warp: BF16/fp32 staging + TMA store issue of a tile
+  kProfEpiStoreWait = 7,        // promotion warp: wait for the previous tile's store to read smem
+  kProfKBlocks = 8,             // count: K blocks promoted (first promotion warp)
+  kProfTiles = 9,               // count: output tiles stored
+  kProfCtas = 10,               // count: CTAs
+  kProfSlots = 16,
+};
+
 // Test-only failure injection (SM100_WGRAD_DEBUG_INJECT=withhold_first_load):
 // the producer announces its first stage's bytes without issuing the copy.
 constexpr int kInjectWithholdFirstLoad = 1;

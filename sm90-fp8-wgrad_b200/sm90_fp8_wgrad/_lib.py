@@ -152,6 +152,8 @@ def load() -> ctypes.CDLL:
             ctypes.c_void_p, ctypes.c_int64, ctypes.POINTER(Sm100WgradMetaOut), ctypes.c_void_p,
         ]
         lib.sm100_wgrad_build_meta.restype = ctypes.c_int
+        lib.sm100_wgrad_profile_counters.argtypes = [ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32]
+        lib.sm100_wgrad_profile_counters.restype = ctypes.c_int
         lib.sm100_wgrad_device_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
         lib.sm100_wgrad_device_error.restype = ctypes.c_int
         lib.sm100_wgrad_status_string.argtypes = [ctypes.c_int]
@@ -170,6 +172,22 @@ def check(status: int, what: str) -> None:
     """Map a non-zero C status to RuntimeError (the reference's error type)."""
     if int(status) != OK:
         raise RuntimeError(f"{what} failed: status {int(status)} ({status_string(status)})")
+
+
+PROFILE_SLOTS = ("producer_wait_stage", "producer_wait_scales", "mma_wait", "mma_issue", "epi_wait",
+                 "epi_promote", "epi_store", "epi_store_wait", "k_blocks", "tiles", "ctas")
+
+
+def profile_counters() -> dict[str, int] | None:
+    """Per-role cycle counters of the grouped GEMM since the last call (read and
+    cleared), or None when the loaded library was built without WGRAD_PROFILE
+    (build one with ``build_ext.py --profile`` and point SM100_WGRAD_LIB at it)."""
+    buf = (ctypes.c_uint64 * 16)()
+    status = load().sm100_wgrad_profile_counters(buf, 16)
+    if int(status) == ERR_UNSUPPORTED:
+        return None
+    check(status, "sm100_wgrad_profile_counters")
+    return {name: int(buf[i]) for i, name in enumerate(PROFILE_SLOTS)}
 
 
 def device_error() -> int:

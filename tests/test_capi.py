@@ -78,3 +78,9 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "_lib", None)
     with pytest.raises(RuntimeError, match="not found"):
         _lib.load()
+
+
+def test_profile_counters_unsupported_in_product_build():
+    """The product library has no timing code: the counter read reports
+    SM100_WGRAD_ERR_UNSUPPORTED (no CUDA call is made)."""
+    assert _lib.profile_counters() is None
