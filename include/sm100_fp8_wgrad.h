@@ -62,6 +62,7 @@ extern "C" {
 #define SM100_WGRAD_TILE_128x128 2
 #define SM100_WGRAD_TILE_128x256_W8 3
 #define SM100_WGRAD_TILE_128x256_W16 4
+#define SM100_WGRAD_TILE_128x128_2CTA 5   /* 128x128 tile, two CTAs (pipelines) per SM */
 
 typedef struct Sm100WgradArgs {
   const void* lhs_data;      /* FP8 e4m3 [M][lhs_pitch]                              */

@@ -70,35 +70,41 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // scale block == K block, bytes per row of an FP8 tile
-constexpr int STAGES = 3;
 constexpr int SCALE_STAGES = 6;
 constexpr int FIRST_EPI_WARP = 4;
 
-// Promotion warps: EPI = 8 or 16 (two or four per TMEM lane quarter); each owns
-// 32 rows x BN / (EPI / 4) columns. 16 warps keep more TMEM loads, scale loads
-// and output stores in flight (better for short-K, HBM-bound launches); 8 warps
-// carry fewer per-warp fixed costs (better for long K).
-// Register split: the launch gives THREADS x (65536 / THREADS rounded down to
-// 8) registers; warpgroup 0 drops to REGS_CONTROL and the promotion warps take
-// the rest: 16 warps: 640 x 96 = 128 x 32 + 512 x 112;
-//            8 warps: 384 x 168 >= 128 x 56 + 256 x 224.
+// Promotion warps: EPI = 4, 8 or 16 (one, two or four per TMEM lane quarter);
+// each owns 32 rows x BN / (EPI / 4) columns. 16 warps keep more TMEM loads,
+// scale loads and output stores in flight (better for short-K, HBM-bound
+// launches); 8 warps carry fewer per-warp fixed costs (better for long K).
+// EPI = 4 (with BN = 128) runs two CTAs per SM: two independent pipelines on
+// different tiles whose promotion warps share each SM sub-partition, so the
+// stalls of one fill the FMA pipe with the other's work.
+// Register split: the launch gives THREADS x (65536 / (THREADS x CTAs per SM)
+// rounded down to 8) registers; warpgroup 0 drops to REGS_CONTROL and the
+// promotion warps take the rest: 16 warps: 640 x 96 = 128 x 32 + 512 x 112;
+// 8 warps: 384 x 168 >= 128 x 56 + 256 x 224; 4 warps, 2 CTAs: 256 x 128 =
+// 128 x 56 + 128 x 200.
 template <int BN, int EPI>
 struct Cfg {
   static constexpr int EPI_WARPS = EPI;
   static constexpr int THREADS = 32 * (4 + EPI_WARPS);
+  static constexpr int CTAS_PER_SM = EPI_WARPS == 4 ? 2 : 1;
+  static constexpr int STAGES = EPI_WARPS == 4 ? 2 : 3;
   static constexpr uint32_t REGS_CONTROL = EPI_WARPS == 16 ? 32 : 56;
-  static constexpr uint32_t REGS_EPILOGUE = EPI_WARPS == 16 ? 112 : 224;
+  static constexpr uint32_t REGS_EPILOGUE = EPI_WARPS == 16 ? 112 : (EPI_WARPS == 4 ? 200 : 224);
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int SCALE_FLOATS = BM + BN;
   static constexpr int COLS_PER_WARP = BN / (EPI_WARPS / 4);  // EPI_WARPS / 4 column groups
-  static constexpr int CHUNK = COLS_PER_WARP >= 128 ? 32 : 16;  // tcgen05.ld columns per load
+  static constexpr int CHUNK = COLS_PER_WARP >= 128 && REGS_EPILOGUE >= 224 ? 32 : 16;  // tcgen05.ld columns
   static constexpr int CHUNKS = COLS_PER_WARP / CHUNK;
   static constexpr int OUT_STAGE_BYTES_PER_WARP = COLS_PER_WARP * 32 * 2 >= 8192 ? 8192 : 4096;
   static constexpr int TMEM_COLS = 2 * BN;          // double-buffered partial
   static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + EPI_WARPS * OUT_STAGE_BYTES_PER_WARP +
                                     SCALE_STAGES * SCALE_FLOATS * 4 + 256 /*barriers*/ + 1024 /*align*/;
-  static_assert(128 * REGS_CONTROL + 32 * EPI_WARPS * REGS_EPILOGUE <= THREADS * ((65536 / THREADS) & ~7),
+  static_assert(128 * REGS_CONTROL + 32 * EPI_WARPS * REGS_EPILOGUE <=
+                    THREADS * ((65536 / (THREADS * CTAS_PER_SM)) & ~7),
                 "register split exceeds the launch allocation");
 };
 
@@ -134,20 +140,20 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, int tile) 
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
+__global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_SM)
     grouped_wgrad_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                          const __grid_constant__ CUtensorMap tmap_out, const GemmParams p) {
   using C = Cfg<BN, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
-  uint8_t* s_b = s_a + STAGES * C::A_BYTES;
-  uint8_t* s_out = s_b + STAGES * C::B_BYTES;
+  uint8_t* s_b = s_a + C::STAGES * C::A_BYTES;
+  uint8_t* s_out = s_b + C::STAGES * C::B_BYTES;
   float* s_scale = reinterpret_cast<float*>(s_out + C::EPI_WARPS * C::OUT_STAGE_BYTES_PER_WARP);
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_scale + SCALE_STAGES * C::SCALE_FLOATS);
-  uint64_t* full_bar = bars;                          // [STAGES]   TMA -> MMA
-  uint64_t* empty_bar = full_bar + STAGES;            // [STAGES]   MMA -> TMA
-  uint64_t* sfull_bar = empty_bar + STAGES;           // [SCALE_STAGES] TMA -> epilogue
+  uint64_t* full_bar = bars;                          // [C::STAGES]   TMA -> MMA
+  uint64_t* empty_bar = full_bar + C::STAGES;            // [C::STAGES]   MMA -> TMA
+  uint64_t* sfull_bar = empty_bar + C::STAGES;           // [SCALE_STAGES] TMA -> epilogue
   uint64_t* sempty_bar = sfull_bar + SCALE_STAGES;    // [SCALE_STAGES] epilogue -> TMA
   uint64_t* tfull_bar = sempty_bar + SCALE_STAGES;    // [2] MMA -> epilogue
   uint64_t* tempty_bar = tfull_bar + 2;               // [2] epilogue -> MMA
@@ -163,7 +169,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
 #endif
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) {
+    for (int i = 0; i < C::STAGES; ++i) {
       mbar_init(&full_bar[i], 1);
       mbar_init(&empty_bar[i], 1);
     }
@@ -220,7 +226,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
             tma_load_2d(s_a + stage * C::A_BYTES, &tmap_a, &full_bar[stage], krow0 + kb * BK, tc.m0);
             tma_load_2d(s_b + stage * C::B_BYTES, &tmap_b, &full_bar[stage], krow0 + kb * BK, tc.n0);
           }
-          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
 
           WGRAD_PROF_T(tw1);
           ok = mbar_wait(&sempty_bar[sstage], sphase ^ 1u, abort_flag, kDevTimeoutProducer);
@@ -276,7 +282,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, 1)
         }
         __syncwarp();
         WGRAD_PROF_ADD(kProfMmaIssue, tm1);
-        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         acc ^= 1;
         if (acc == 0) aphase ^= 1u;
       }
@@ -474,7 +480,8 @@ cudaError_t launch_grouped_wgrad(const CUtensorMap& ta, const CUtensorMap& tb, c
     return p.epi_warps == 16 ? launch_impl<256, 16>(ta, tb, to, p, grid, stream)
                              : launch_impl<256, 8>(ta, tb, to, p, grid, stream);
   }
-  return launch_impl<128, 8>(ta, tb, to, p, grid, stream);
+  return p.epi_warps == 4 ? launch_impl<128, 4>(ta, tb, to, p, grid, stream)
+                          : launch_impl<128, 8>(ta, tb, to, p, grid, stream);
 }
 
 }  // namespace wgrad

@@ -138,7 +138,7 @@ def test_quantiser_fp32_input_and_odd_columns(cuda_device):
     np.testing.assert_array_equal(op.scales.cpu().numpy().view(np.uint32), ref.scales.view(np.uint32))
 
 
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x128", "sm100_128x256_w8", "sm100_128x256_w16"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x128", "sm100_128x256_w8", "sm100_128x256_w16", "sm100_128x128_2cta"])
 @pytest.mark.parametrize("case", sorted(SMALL_CASES) + ["c1"])
 def test_grouped_wgrad_matches_oracle(cuda_device, case, tuned_config):
     from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
@@ -159,7 +159,7 @@ def test_grouped_wgrad_matches_oracle(cuda_device, case, tuned_config):
     assert _lib.device_error() == 0
 
 
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w8", "sm100_128x256_w16"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w8", "sm100_128x256_w16", "sm100_128x128_2cta"])
 def test_grouped_wgrad_fp32_out_and_accumulate(cuda_device, tuned_config):
     from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
 
@@ -185,7 +185,7 @@ def test_grouped_wgrad_fp32_out_and_accumulate(cuda_device, tuned_config):
     np.testing.assert_allclose(got, expect, rtol=2 ** -7, atol=1e-5 * float(np.abs(expect).max()))
 
 
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta"])
 @pytest.mark.parametrize("hidden,inter", [(144, 80), (272, 48), (512, 128)])
 def test_grouped_wgrad_ragged_tiles(cuda_device, hidden, inter, tuned_config):
     """M, N not multiples of the 128 x 256 tile; empty experts; long K."""
