@@ -394,6 +394,7 @@ def main(argv: list[str] | None = None) -> int:
 
     if not torch.cuda.is_available():
         raise RuntimeError("the matrix run needs a CUDA device")
+    own_group = False
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         import torch.distributed as dist
 
@@ -401,6 +402,7 @@ def main(argv: list[str] | None = None) -> int:
         torch.cuda.set_device(local)
         if not dist.is_initialized():
             dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+            own_group = True
     device = torch.device("cuda", torch.cuda.current_device())
     rank, _ = _dist_world()
     out_dir = Path(a.output_dir)
@@ -423,6 +425,10 @@ def main(argv: list[str] | None = None) -> int:
                   f"{'ok' if row['passed'] else 'FAIL'}", flush=True)
     if rank == 0:
         (out_dir / "results.md").write_text(render_markdown(load_rows(results)))
+    if own_group:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
     return 0 if all(r["passed"] for r in rows) else 1
 
 
