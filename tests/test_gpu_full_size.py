@@ -21,6 +21,8 @@ pytestmark = pytest.mark.gpu
 
 # name: (experts, top_k, hidden, intermediate, tokens, route, shards)
 CONFIGS = {
+    "dsv3_32k": (256, 8, 7168, 2048, 32768, "uniform", 1),
+    "dsv3_4k": (256, 8, 7168, 2048, 4096, "uniform", 1),
     "qwen3_32k": (128, 8, 2048, 768, 32768, "uniform", 1),
     "dsv3_skewed_32k": (256, 8, 7168, 2048, 32768, "zipf", 1),
     "large_expert_16k_shard": (32, 2, 6144, 9216, 16384, "zipf", 8),
@@ -29,10 +31,11 @@ CONFIGS = {
 
 
 def _dequant(op, k0: int, k1: int, b0: int) -> torch.Tensor:
-    """fp32 [rows, cols] of the padded operand rows k0..k1 (blocks from b0)."""
+    """fp32 [rows, cols] of operand rows k0..k1 (blocks from b0): whole 128-row
+    blocks in the padded layout, valid rows only in the packed layout."""
     rows = op.data[k0:k1].float()
-    nb = (k1 - k0) // 128
-    scale = op.scales[b0:b0 + nb].repeat_interleave(128, dim=0)
+    nb = (k1 - k0 + 127) // 128
+    scale = op.scales[b0:b0 + nb].repeat_interleave(128, dim=0)[: k1 - k0]
     return rows * scale
 
 
@@ -45,8 +48,9 @@ def _calc_diff(x: torch.Tensor, y: torch.Tensor) -> float:
     return float(1.0 - 2.0 * (x * y).sum() / denom)
 
 
-@pytest.mark.parametrize("name", sorted(CONFIGS))
-def test_full_size_sampled_experts(cuda_device, name):
+@pytest.mark.parametrize("name,layout", [(n, "padded") for n in sorted(CONFIGS)] +
+                         [("dsv3_skewed_32k", "packed"), ("many_small_32k_shard", "packed")])
+def test_full_size_sampled_experts(cuda_device, name, layout):
     from sm90_fp8_wgrad.routing import make_routing, shard_experts
     from sm90_fp8_wgrad.synthetic import make_synthetic_wgrad_inputs, run_custom_down, run_custom_gate_up
 
@@ -55,14 +59,14 @@ def test_full_size_sampled_experts(cuda_device, name):
     e0, e1 = shard_experts(experts, shards, 0)
     inp = make_synthetic_wgrad_inputs(tokens=tokens, experts=experts, top_k=top_k, hidden=hidden,
                                       intermediate=inter, route=route, seed=1234, device=cuda_device,
-                                      expert_range=(e0, e1), routing=routing)
+                                      expert_range=(e0, e1), routing=routing, layout_mode=layout)
     inp.drop_sources()
     run_custom_down(inp)
     run_custom_gate_up(inp)
     torch.cuda.synchronize()
 
     counts = inp.counts
-    cu = inp.meta.padded_cu_seqlens_k.cpu().tolist()
+    cu = (inp.meta.padded_cu_seqlens_k if layout == "padded" else inp.meta.cu_seqlens_k).cpu().tolist()
     bo = inp.meta.block_offsets.cpu().tolist()
     nonempty = [e for e, c in enumerate(counts) if c > 0]
     sample = {max(nonempty, key=lambda e: counts[e]), min(nonempty, key=lambda e: counts[e]),
@@ -77,6 +81,6 @@ def test_full_size_sampled_experts(cuda_device, name):
             got = out[e].float()
             assert torch.isfinite(got).all()
             cd = _calc_diff(got, ref)
-            assert cd <= 1e-5, (name, e, counts[e], cd)
+            assert cd <= 1e-5, (name, layout, e, counts[e], cd)
     for e in empty:
         assert not inp.down_out_bf16[e].any() and not inp.gate_up_out_bf16[e].any(), (name, e)
