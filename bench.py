@@ -70,56 +70,110 @@ def measured_peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock and throttle reasons sampled during the timed region.
 
+    In-process NVML (read-only queries) every ~10 ms from a background thread,
+    started right before the first timed launch and stopped after the final
+    synchronize, so every sample lies inside the timed region; the device is
+    matched to the CUDA device by PCI bus id. Falls back to ``nvidia-smi -lms
+    100`` when NVML is unavailable."""
+
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, dev: torch.device, gpu_index: int):
+        self.dev = dev
         self.gpu_index = gpu_index
         self.proc = None
+        self.thread = None
         self.lines: list[str] = []
+        self.rows: list[tuple[float, float, list[str]]] = []
+        self.stop_flag = threading.Event()
+        self.nvml = None
+        self.handle = None
+
+    def _nvml_handle(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.dev)
+        bus = getattr(props, "pci_bus_id", None)
+        if bus is not None:
+            bus_id = f"{getattr(props, 'pci_domain_id', 0):08X}:{bus:02X}:{getattr(props, 'pci_device_id', 0):02X}.0"
+            try:
+                return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus_id)
+            except pynvml.NVMLError:
+                pass
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu_index)
+
+    def _nvml_loop(self) -> None:
+        nv, h = self.nvml, self.handle
+        bits = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+        max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        while not self.stop_flag.is_set():
+            try:
+                mhz = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                reasons = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.rows.append((mhz, max_mhz, ["active" if reasons & b else "not active" for b in bits]))
+            except Exception:
+                break
+            time.sleep(0.01)
 
     def start(self) -> None:
         try:
+            self.nvml, self.handle = self._nvml_handle()
+            self.thread = threading.Thread(target=self._nvml_loop, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.nvml = None
+        try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
                  "-i", str(self.gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self._t = threading.Thread(target=self._read, daemon=True)
-            self._t.start()
+            self.thread = threading.Thread(target=self._read_smi, daemon=True)
+            self.thread.start()
         except Exception:
             self.proc = None
 
-    def _read(self) -> None:
+    def _read_smi(self) -> None:
         assert self.proc is not None and self.proc.stdout is not None
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self) -> dict | None:
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        rows = []
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
+        source = "nvml"
+        if self.nvml is not None:
+            self.stop_flag.set()
+            if self.thread is not None:
+                self.thread.join(timeout=2)
+        elif self.proc is not None:
+            source = "nvidia-smi"
+            self.proc.terminate()
             try:
-                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
-            except ValueError:
-                continue
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            for ln in self.lines:
+                parts = [x.strip() for x in ln.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    self.rows.append((float(parts[1]), float(parts[2]), [p.lower() for p in parts[5:9]]))
+                except ValueError:
+                    continue
+        else:
+            return None
+        rows = self.rows
         if not rows:
             return None
         mhz = sorted(r[0] for r in rows)
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[2]) if v.lower() == "active"})
+        reasons = sorted({self.NAMES[i] for r in rows for i, v in enumerate(r[2]) if v.lower() == "active"})
         return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows), "sm_mhz_min": mhz[0], "source": source}
 
 
 def flops_of(inp) -> tuple[float, float]:
@@ -305,11 +359,10 @@ def run_ours(args) -> None:
 
     stream = torch.cuda.current_stream(dev)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    clocks = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else
+    clocks = ClockSampler(dev, dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else
                           int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank]))
-    clocks.start()
-    time.sleep(0.3)
     _barrier(world, dev)
+    clocks.start()
     for s in range(args.steps):
         evs[s][0].record(stream)
         run_custom_down(inp)
@@ -317,8 +370,8 @@ def run_ours(args) -> None:
         run_custom_gate_up(inp)
         evs[s][2].record(stream)
     torch.cuda.synchronize(dev)
-    _barrier(world, dev)
     clk = clocks.stop()
+    _barrier(world, dev)
     total_ms = evs[0][0].elapsed_time(evs[-1][2])
     down_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
     gate_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
