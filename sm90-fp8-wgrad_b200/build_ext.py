@@ -2,9 +2,11 @@
 
 Usage: python sm90-fp8-wgrad_b200/build_ext.py [--force] [--profile]
 Output: sm90-fp8-wgrad_b200/sm90_fp8_wgrad/_lib/libsm100_fp8_wgrad.so
-        (--profile: libsm100_fp8_wgrad_profile.so, the same library with the
-        GEMM's per-role cycle counters compiled in, -DWGRAD_PROFILE=1; load it
-        with SM100_WGRAD_LIB=<path> and read sm90_fp8_wgrad._lib.profile_counters())
+        (--profile: libsm100_fp8_wgrad_profile.so with the GEMM's per-role cycle
+        counters, -DWGRAD_PROFILE=1, read with sm90_fp8_wgrad._lib.profile_counters();
+        --debug-modes: libsm100_fp8_wgrad_debug.so with the known-answer kernel
+        modes of KERNEL_LAB_WGRAD_KERNEL_MODE, -DWGRAD_DEBUG_MODES=1. Load either
+        with SM100_WGRAD_LIB=<path>.)
 """
 from __future__ import annotations
 
@@ -19,6 +21,7 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 OUT = HERE / "sm90_fp8_wgrad" / "_lib" / "libsm100_fp8_wgrad.so"
 OUT_PROFILE = HERE / "sm90_fp8_wgrad" / "_lib" / "libsm100_fp8_wgrad_profile.so"
+OUT_DEBUG = HERE / "sm90_fp8_wgrad" / "_lib" / "libsm100_fp8_wgrad_debug.so"
 SOURCES = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [HERE.parent / "include" / "sm100_fp8_wgrad.h"]
 
 
@@ -36,8 +39,8 @@ def needs_build(out: Path = OUT) -> bool:
     return any(s.stat().st_mtime > mtime for s in SOURCES)
 
 
-def build(force: bool = False, verbose: bool = False, profile: bool = False) -> Path:
-    out = OUT_PROFILE if profile else OUT
+def build(force: bool = False, verbose: bool = False, profile: bool = False, debug_modes: bool = False) -> Path:
+    out = OUT_DEBUG if debug_modes else (OUT_PROFILE if profile else OUT)
     if not force and not needs_build(out):
         return out
     out.parent.mkdir(parents=True, exist_ok=True)
@@ -46,6 +49,7 @@ def build(force: bool = False, verbose: bool = False, profile: bool = False) -> 
         nvcc_path(), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
         "-shared", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-Xptxas", "-v" if verbose else "-O3",
         *(["-DWGRAD_PROFILE=1"] if profile else []),
+        *(["-DWGRAD_DEBUG_MODES=1"] if debug_modes else []),
         "-o", str(tmp), str(CSRC / "unity.cu"),
     ]
     res = subprocess.run(cmd, capture_output=True, text=True)
@@ -62,5 +66,6 @@ if __name__ == "__main__":
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--profile", action="store_true", help="build the per-role cycle-counter library")
+    ap.add_argument("--debug-modes", action="store_true", help="build the known-answer kernel-mode library")
     a = ap.parse_args()
-    print(build(force=a.force, verbose=a.verbose, profile=a.profile))
+    print(build(force=a.force, verbose=a.verbose, profile=a.profile, debug_modes=a.debug_modes))

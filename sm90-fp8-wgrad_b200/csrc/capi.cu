@@ -214,6 +214,18 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   p.accumulate = a->accumulate != 0;
   p.has_operands = has_operands ? 1 : 0;
   p.epi_warps = pick_epi_warps(a->tile_config, bn, a->total_blocks, a->num_experts);
+  // Known-answer kernel modes (KERNEL_LAB_WGRAD_KERNEL_MODE, as the reference):
+  // honoured by instrumented builds only; the product build refuses them.
+  p.mode = wgrad::kModeNormal;
+  if (const char* km = std::getenv("KERNEL_LAB_WGRAD_KERNEL_MODE"); km != nullptr && km[0] != '\0' &&
+      std::strcmp(km, "normal") != 0) {
+    if (std::strcmp(km, "coord_m") == 0) p.mode = wgrad::kModeCoordM;
+    else if (std::strcmp(km, "coord_n") == 0) p.mode = wgrad::kModeCoordN;
+    else if (std::strcmp(km, "scale_only") == 0) p.mode = wgrad::kModeScaleOnly;
+    else if (std::strcmp(km, "unscaled") == 0) p.mode = wgrad::kModeUnscaled;
+    else return SM100_WGRAD_ERR_INVALID_ARG;
+    if (!WGRAD_DEBUG_MODES) return SM100_WGRAD_ERR_UNSUPPORTED;
+  }
   // Test-only failure injection of the bounded-wait path (never set in normal use).
   const char* inject = std::getenv("SM100_WGRAD_DEBUG_INJECT");
   p.inject = (inject != nullptr && std::strcmp(inject, "withhold_first_load") == 0) ? wgrad::kInjectWithholdFirstLoad : 0;

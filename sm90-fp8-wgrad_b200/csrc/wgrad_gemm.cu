@@ -317,7 +317,13 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
         if (!ok) break;
         tc_fence_after();
         const float* sc = s_scale + sstage * C::SCALE_FLOATS;
+#if WGRAD_DEBUG_MODES
+        const bool unit_scales = p.mode == kModeUnscaled;  // raw FP8 product only
+        const bool unit_raw = p.mode == kModeScaleOnly;    // scale product only
+        const float a_s = unit_scales ? 1.f : sc[row];
+#else
         const float a_s = sc[row];
+#endif
         const float* b_s = sc + BM + half * C::COLS_PER_WARP;
         const uint32_t t_addr = tmem_base + lane_addr + static_cast<uint32_t>(acc * BN + half * C::COLS_PER_WARP);
         // Software pipeline over 32-column chunks: the TMEM load of chunk c+1
@@ -338,8 +344,16 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
           }
 #pragma unroll
           for (int j = 0; j < CH; j += 4) {
+#if WGRAD_DEBUG_MODES
+            const float4 sb4 = unit_scales ? make_float4(1.f, 1.f, 1.f, 1.f)
+                                           : *reinterpret_cast<const float4*>(b_s + c * CH + j);
+            const uint32_t one = __float_as_uint(1.f);
+            const uint32_t q[4] = {unit_raw ? one : r[c & 1][j], unit_raw ? one : r[c & 1][j + 1],
+                                   unit_raw ? one : r[c & 1][j + 2], unit_raw ? one : r[c & 1][j + 3]};
+#else
             const float4 sb4 = *reinterpret_cast<const float4*>(b_s + c * CH + j);
             const uint32_t* q = &r[c & 1][j];
+#endif
             float u0, u1, u2, u3;
             mul_f32x2(u0, u1, __uint_as_float(q[0]), __uint_as_float(q[1]), sb4.x, sb4.y);
             mul_f32x2(u2, u3, __uint_as_float(q[2]), __uint_as_float(q[3]), sb4.z, sb4.w);
@@ -363,6 +377,16 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
       WGRAD_PROF_INC(kProfTiles);
       const int g_row = tc.m0 + row;
       const int col0 = tc.n0 + half * C::COLS_PER_WARP;
+#if WGRAD_DEBUG_MODES
+      if (p.mode == kModeCoordM || p.mode == kModeCoordN || p.mode == kModeScaleOnly) {
+#pragma unroll
+        for (int j = 0; j < C::COLS_PER_WARP; ++j) {
+          fin[j] = p.mode == kModeCoordM ? static_cast<float>(g_row)
+                 : p.mode == kModeCoordN ? static_cast<float>(col0 + j)
+                                         : fin[j] * 1048576.0f;  // 2^20, as the reference
+        }
+      }
+#endif
       if (p.accumulate) {
         const bool row_ok = g_row < p.m;
         const size_t base = (static_cast<size_t>(tc.e) * p.m + (row_ok ? g_row : 0)) * p.n;

@@ -28,6 +28,17 @@ enum ProfSlot : int {
   kProfSlots = 16,
 };
 
+#ifndef WGRAD_DEBUG_MODES
+#define WGRAD_DEBUG_MODES 0
+#endif
+
+// Known-answer kernel modes (instrumented builds only, -DWGRAD_DEBUG_MODES=1),
+// selected like the reference's KERNEL_LAB_WGRAD_KERNEL_MODE (gemm_sm90.py:139-175):
+//   coord_m / coord_n  out[e, m, n] = m / n            (pins the tile -> output mapping)
+//   scale_only         out = 2^20 * sum_b sa[b,m] sb[b,n]  (pins scale indexing, :5271-5292)
+//   unscaled           out = sum_k A[m,k] B[n,k]       (the FP8 product alone, :2820-2868)
+enum KernelMode : int { kModeNormal = 0, kModeCoordM = 1, kModeCoordN = 2, kModeScaleOnly = 3, kModeUnscaled = 4 };
+
 // Test-only failure injection (SM100_WGRAD_DEBUG_INJECT=withhold_first_load):
 // the producer announces its first stage's bytes without issuing the copy.
 constexpr int kInjectWithholdFirstLoad = 1;
@@ -50,6 +61,7 @@ struct GemmParams {
   int has_operands;             // 0 when the operand K extent is empty
   int epi_warps;                // promotion warps: 8, or 16 (bn 256 only)
   int inject;                   // test-only failure injection (kInject*), 0 in normal use
+  int mode;                     // KernelMode; only instrumented builds honour a non-zero mode
 };
 
 cudaError_t launch_grouped_wgrad(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,

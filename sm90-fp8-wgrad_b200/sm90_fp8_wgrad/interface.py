@@ -65,6 +65,23 @@ TUNED_CONFIGS: dict[str, int] = {
 }
 
 
+# KERNEL_LAB_WGRAD_KERNEL_MODE values (reference gemm_sm90.py:139-175) with a B200
+# counterpart: the known-answer modes, honoured by the debug-modes library
+# (build_ext.py --debug-modes). The reference's other values select variants of
+# the SM90 kernel's structure and have no meaning here.
+B200_KERNEL_MODES = ("normal", "coord_m", "coord_n", "scale_only", "unscaled")
+
+
+def _kernel_mode() -> str:
+    mode = os.environ.get("KERNEL_LAB_WGRAD_KERNEL_MODE", "").strip()
+    if mode and mode not in B200_KERNEL_MODES:
+        raise RuntimeError(
+            f"KERNEL_LAB_WGRAD_KERNEL_MODE={mode!r} selects an SM90 kernel variant with no B200 counterpart; "
+            f"B200 modes: {', '.join(B200_KERNEL_MODES)}"
+        )
+    return mode or "normal"
+
+
 def _check_fp8_operand(name: str, operand: Fp8GroupedWgradOperand) -> None:
     """Operand checks of the reference (interface.py:28-69)."""
     if operand.data.dtype != torch.float8_e4m3fn:
@@ -141,6 +158,7 @@ def fp8_grouped_wgrad_sm90(
     corresponding slice of a full launch. It lets a caller overlap the
     device-to-host copy of finished experts with the rest of the GEMM.
     """
+    kernel_mode = _kernel_mode()
     layout_mode = resolve_wgrad_layout_mode()
     _check_fp8_operand("lhs", lhs)
     _check_fp8_operand("rhs", rhs)
@@ -256,6 +274,11 @@ def fp8_grouped_wgrad_sm90(
     lib = _lib.load()
     with torch.cuda.device(dev):
         status = lib.sm100_fp8_grouped_wgrad(ctypes.byref(args), torch.cuda.current_stream().cuda_stream)
+    if int(status) == _lib.ERR_UNSUPPORTED and kernel_mode != "normal":
+        raise RuntimeError(
+            f"kernel mode {kernel_mode!r} needs the debug-modes library: build it with "
+            "`python sm90-fp8-wgrad_b200/build_ext.py --debug-modes` and load it with SM100_WGRAD_LIB=<path>"
+        )
     _lib.check(status, "sm100_fp8_grouped_wgrad")
     return out
 

@@ -84,3 +84,13 @@ def test_profile_counters_unsupported_in_product_build():
     """The product library has no timing code: the counter read reports
     SM100_WGRAD_ERR_UNSUPPORTED (no CUDA call is made)."""
     assert _lib.profile_counters() is None
+
+
+def test_sm90_only_kernel_modes_rejected(monkeypatch):
+    """KERNEL_LAB_WGRAD_KERNEL_MODE values that select SM90 kernel variants are
+    refused before anything touches the GPU."""
+    from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
+
+    monkeypatch.setenv("KERNEL_LAB_WGRAD_KERNEL_MODE", "tma_only")
+    with pytest.raises(RuntimeError, match="no B200 counterpart"):
+        fp8_grouped_wgrad_sm90(None, None, None, None)
