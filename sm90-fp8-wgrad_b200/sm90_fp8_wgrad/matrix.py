@@ -148,8 +148,11 @@ def _calc_diff(x, y) -> float:
     return 0.0 if denom == 0.0 else 1.0 - 2.0 * float((x * y).sum()) / denom
 
 
-def _check_rank(inp, layout: str) -> tuple[float, bool]:
-    """Max calc_diff over the sampled experts; empty experts must be zero.
+def check_sampled_experts(inp, layout: str) -> tuple[float, bool]:
+    """Max calc_diff over the sampled experts (longest and shortest non-empty)
+    against an fp32 dequantise-then-matmul of the same FP8 operands (the
+    reference's ref_scaled_wgrad, checks.py:42-61); second value: every output
+    is finite and every empty expert is exactly zero.
     An expert's operand rows start at padded_cu_seqlens_k[e] in the padded
     layout and at cu_seqlens_k[e] (valid rows only) in the packed layout."""
     import torch
@@ -203,7 +206,7 @@ def run_rank(case: Case, routing, expert_range, local_tokens: int, *, seed: int,
         timing[name] = stats.to_dict()
     run_custom_total(inp, tuned_config=tuned_config)
     torch.cuda.synchronize()
-    diff, zeros_ok = _check_rank(inp, layout)
+    diff, zeros_ok = check_sampled_experts(inp, layout)
     rows = inp.valid_rows
     padded = int(inp.meta.padded_rows)
     blocks = int(inp.meta.total_blocks)
