@@ -190,11 +190,13 @@ def validate_outputs(inp, layout: str, world: int, dev) -> dict:
     ranks."""
     from sm90_fp8_wgrad.matrix import check_sampled_experts
 
-    diff, zeros_ok = check_sampled_experts(inp, layout)
+    diff, zeros_ok, rel = check_sampled_experts(inp, layout, with_rel_err=True)
     finite = _all_finite(inp.down_out_bf16) and _all_finite(inp.gate_up_out_bf16)
     diff = _max_over_ranks(diff if math.isfinite(diff) else 1e30, world, dev)
+    rel = _max_over_ranks(rel if math.isfinite(rel) else 1e30, world, dev)
     bad = _max_over_ranks(0.0 if (finite and zeros_ok) else 1.0, world, dev)
-    return {"calc_diff_max": diff, "calc_diff_gate": 1e-5, "finite_and_empty_zero": bad == 0.0,
+    return {"calc_diff_max": diff, "calc_diff_gate": 1e-5, "max_rel_err_normwise": rel,
+            "finite_and_empty_zero": bad == 0.0,
             "passed": bool(bad == 0.0 and diff <= 1e-5)}
 
 

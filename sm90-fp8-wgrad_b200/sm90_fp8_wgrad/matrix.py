@@ -148,19 +148,23 @@ def _calc_diff(x, y) -> float:
     return 0.0 if denom == 0.0 else 1.0 - 2.0 * float((x * y).sum()) / denom
 
 
-def check_sampled_experts(inp, layout: str) -> tuple[float, bool]:
+def check_sampled_experts(inp, layout: str, with_rel_err: bool = False):
     """Max calc_diff over the sampled experts (longest and shortest non-empty)
     against an fp32 dequantise-then-matmul of the same FP8 operands (the
-    reference's ref_scaled_wgrad, checks.py:42-61); second value: every output
-    is finite and every empty expert is exactly zero.
+    reference's ref_scaled_wgrad, checks.py:42-61); second value: every sampled
+    output is finite and every empty expert is exactly zero. With
+    ``with_rel_err`` a third value: the largest normwise relative error
+    max|out - ref| / max|ref| over the sampled experts.
     An expert's operand rows start at padded_cu_seqlens_k[e] in the padded
     layout and at cu_seqlens_k[e] (valid rows only) in the packed layout."""
     import torch
 
     counts = inp.counts
     nonempty = [e for e, c in enumerate(counts) if c > 0]
+    zeros_ok = all(not inp.down_out_bf16[e].any() and not inp.gate_up_out_bf16[e].any()
+                   for e, c in enumerate(counts) if c == 0)
     if not nonempty:
-        return 0.0, bool(not inp.down_out_bf16.any() and not inp.gate_up_out_bf16.any())
+        return (0.0, zeros_ok, 0.0) if with_rel_err else (0.0, zeros_ok)
     sample = sorted({max(nonempty, key=lambda e: counts[e]), min(nonempty, key=lambda e: counts[e])})
     cu = (inp.meta.padded_cu_seqlens_k if layout == "padded" else inp.meta.cu_seqlens_k).cpu().tolist()
     bo = inp.meta.block_offsets.cpu().tolist()
@@ -170,7 +174,7 @@ def check_sampled_experts(inp, layout: str) -> tuple[float, bool]:
         nb = (rows + 127) // 128
         return op.data[k0:k1].float() * op.scales[b0:b0 + nb].repeat_interleave(128, dim=0)[:rows]
 
-    worst = 0.0
+    worst, worst_rel = 0.0, 0.0
     for e in sample:
         k0, k1, b0 = cu[e], cu[e + 1], bo[e]
         for lhs, rhs, out in ((inp.grad_y_q, inp.hidden_q, inp.down_out_bf16),
@@ -178,11 +182,10 @@ def check_sampled_experts(inp, layout: str) -> tuple[float, bool]:
             ref = deq(lhs, k0, k1, b0).t() @ deq(rhs, k0, k1, b0)
             got = out[e].float()
             if not bool(torch.isfinite(got).all()):
-                return math.inf, False
+                return (math.inf, False, math.inf) if with_rel_err else (math.inf, False)
             worst = max(worst, _calc_diff(got, ref))
-    zeros_ok = all(not inp.down_out_bf16[e].any() and not inp.gate_up_out_bf16[e].any()
-                   for e, c in enumerate(counts) if c == 0)
-    return worst, zeros_ok
+            worst_rel = max(worst_rel, float((got - ref).abs().max() / ref.abs().max().clamp_min(1e-30)))
+    return (worst, zeros_ok, worst_rel) if with_rel_err else (worst, zeros_ok)
 
 
 def run_rank(case: Case, routing, expert_range, local_tokens: int, *, seed: int, layout: str, tuned_config: str,
@@ -206,7 +209,7 @@ def run_rank(case: Case, routing, expert_range, local_tokens: int, *, seed: int,
         timing[name] = stats.to_dict()
     run_custom_total(inp, tuned_config=tuned_config)
     torch.cuda.synchronize()
-    diff, zeros_ok = check_sampled_experts(inp, layout)
+    diff, zeros_ok, rel = check_sampled_experts(inp, layout, with_rel_err=True)
     rows = inp.valid_rows
     padded = int(inp.meta.padded_rows)
     blocks = int(inp.meta.total_blocks)
@@ -216,7 +219,7 @@ def run_rank(case: Case, routing, expert_range, local_tokens: int, *, seed: int,
            + e_local * 3 * hidden * inter * 2)
     out = {"valid_rows": rows, "padded_rows": padded, "blocks": blocks, "local_experts": e_local,
            "local_tokens": local_tokens, "flops": flops, "hbm_bytes": hbm, "timing": timing,
-           "calc_diff": diff, "empty_experts_zero": zeros_ok}
+           "calc_diff": diff, "max_rel_err": rel, "empty_experts_zero": zeros_ok}
     del inp
     torch.cuda.empty_cache()
     return out
@@ -261,12 +264,14 @@ def run_case(case: Case, *, ep_mode: str, seed: int, layout: str, tuned_config: 
     step = max(p["timing"]["total"]["mean_ms"] for p in per_rank)
     job_flops = sum(p["flops"] for p in per_rank)
     diff = max(p["calc_diff"] for p in per_rank)
+    rel_err = max(p["max_rel_err"] for p in per_rank)
     zeros_ok = all(p["empty_experts_zero"] for p in per_rank)
     gpus = len(per_rank)
     if concurrent:
         step = _reduce_over_ranks(step, "max")
         job_flops = _reduce_over_ranks(job_flops, "sum")
         diff = _reduce_over_ranks(diff, "max")
+        rel_err = _reduce_over_ranks(rel_err, "max")
         zeros_ok = _reduce_over_ranks(0.0 if zeros_ok else 1.0, "max") == 0.0
         gpus = world
     name, experts, top_k, hidden, inter = MODEL_SPECS[case.model]
@@ -283,7 +288,7 @@ def run_case(case: Case, *, ep_mode: str, seed: int, layout: str, tuned_config: 
         "slowest_rank": slow["rank"], "slowest_rank_hbm_gbs": slow["hbm_bytes"] / (slow["timing"]["total"]["mean_ms"] * 1e-3) / 1e9,
         "imbalance": (step / (sum(p["timing"]["total"]["mean_ms"] for p in per_rank) / len(per_rank))
                       if not concurrent else None),
-        "calc_diff": diff, "diff_gate": diff_gate, "empty_experts_zero": zeros_ok,
+        "calc_diff": diff, "max_rel_err": rel_err, "diff_gate": diff_gate, "empty_experts_zero": zeros_ok,
         "passed": bool(diff <= diff_gate and zeros_ok), "ranks": per_rank if not concurrent else None,
     }
     return row
@@ -308,7 +313,8 @@ def render_markdown(rows: list[dict], *, title: str = "Grouped FP8 Wgrad on B200
     meta = rows[0]
     lines.append(f"Layout `{meta.get('layout')}`, config `{meta.get('tuned_config')}`, "
                  f"EP mode `{meta.get('ep_mode')}`, seed {meta.get('seed')}. Step = down + gate/up "
-                 "Wgrad; FLOPs count valid rows only (6 H I R); EP step time is the slowest rank.")
+                 "Wgrad; FLOPs count valid rows only (6 H I R); EP step time is the slowest rank; "
+                 "max rel err = max|out - ref| / max|ref| over the checked experts.")
     lines.append("")
     by_model: dict[str, list[dict]] = {}
     for r in rows:
@@ -319,14 +325,15 @@ def render_markdown(rows: list[dict], *, title: str = "Grouped FP8 Wgrad on B200
                      f"I={r0['intermediate']})")
         lines.append("")
         lines.append("| route | EP | tokens | step ms | TFLOP/s per GPU | % FP8 peak | slowest-rank HBM GB/s "
-                     "| imbalance | calc_diff | ok |")
-        lines.append("|---|---:|---:|---:|---:|---:|---:|---:|---:|:-:|")
+                     "| imbalance | calc_diff | max rel err | ok |")
+        lines.append("|---|---:|---:|---:|---:|---:|---:|---:|---:|---:|:-:|")
         for r in sorted(rs, key=lambda x: (x["route"], x["ep"], x["tokens"])):
             lines.append(
                 f"| {r['route']} | {r['ep']} | {token_label(r['tokens'])} | {_fmt(r['step_ms'], '.3f')} "
                 f"| {_fmt(r['per_gpu_tflops'], '.0f')} | {_fmt(r.get('pct_fp8_peak'), '.1f')} "
                 f"| {_fmt(r.get('slowest_rank_hbm_gbs'), '.0f')} | {_fmt(r.get('imbalance'), '.2f')} "
-                f"| {_fmt(r['calc_diff'], '.2e')} | {'yes' if r['passed'] else 'NO'} |")
+                f"| {_fmt(r['calc_diff'], '.2e')} | {_fmt(r.get('max_rel_err'), '.1e')} "
+                f"| {'yes' if r['passed'] else 'NO'} |")
         lines.append("")
     return "\n".join(lines)
 
