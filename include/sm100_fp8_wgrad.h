@@ -96,6 +96,12 @@ typedef struct Sm100WgradArgs {
  * packed mode (k_row_offsets = wgmma_cu_seqlens_k, 32-row aligned expert
  * starts, operands = kernel_data with >= 127 zero guard rows); an expert's last
  * scale block multiplies only its ceil(rows / 32) valid 32-row K slices.
+ * A launch over an expert sub-range [e0, e1) passes num_experts = e1 - e0 and
+ * block_offsets / k_row_offsets / out offset by e0 (their values stay absolute).
+ * Environment read per launch: KERNEL_LAB_WGRAD_KERNEL_MODE (the reference's
+ * known-answer modes coord_m / coord_n / scale_only / unscaled; only a library
+ * built with -DWGRAD_DEBUG_MODES=1 runs them, others return
+ * SM100_WGRAD_ERR_UNSUPPORTED) and SM100_WGRAD_DEBUG_INJECT (test-only).
  */
 SM100_WGRAD_API int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* args, void* stream);
 
