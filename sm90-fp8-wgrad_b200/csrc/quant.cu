@@ -23,11 +23,11 @@
 // compact tail operands (quant.py:273-307), 32 or 64 rows: block b then
 // occupies padded rows [block_rows * b, block_rows * (b + 1)).
 //
-// HBM-bound transpose: a CTA owns one scale block x a strip of 128 BF16 (64
-// fp32) columns. Every thread issues its eight 16-byte row loads before
-// writing them to shared memory; then each thread walks one column slice
-// (amax, then x / scale) and writes 16 rows at a time as one 16-byte segment
-// of the K-contiguous operand.
+// HBM-bound transpose: a CTA owns one scale block x a strip of 64 columns.
+// Every thread issues its 16-byte row loads before writing them to shared
+// memory (16 KB BF16 tiles, so eight CTAs share an SM); then each thread walks
+// one column slice (amax, then x / scale), and the FP8 bytes leave through a
+// column-major staging area as full 128-byte lines of the K-contiguous operand.
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -43,13 +43,15 @@ namespace {
 constexpr int QBLOCK_ROWS = 128;
 constexpr int QTHREADS = 256;
 
-// Column strip of one CTA: 16 threads per tile row, one 16-byte vector each
-// (128 BF16 or 64 fp32 columns), eight rows-passes of 16 rows.
+// Column strip of one CTA: 64 columns (a 16 KB BF16 or 32 KB fp32 tile);
+// TPR threads per tile row, one 16-byte vector each, ROW_PASSES passes.
 template <typename T>
 struct QTile {
   static constexpr int VEC = 16 / static_cast<int>(sizeof(T));
-  static constexpr int COLS = 16 * VEC;
-  static constexpr int ROW_PASSES = QBLOCK_ROWS / (QTHREADS / 16);
+  static constexpr int COLS = 64;
+  static constexpr int TPR = COLS / VEC;                      // threads per tile row
+  static constexpr int ROWS_PER_PASS = QTHREADS / TPR;
+  static constexpr int ROW_PASSES = QBLOCK_ROWS / ROWS_PER_PASS;
   static constexpr int PARTS = QTHREADS / COLS;               // row parts per column
   static constexpr int ROWS_PER_PART = QBLOCK_ROWS / PARTS;   // 64 (bf16) or 32 (fp32)
 };
@@ -103,7 +105,7 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
                                                                   float* __restrict__ scales, bool vec_ok,
                                                                   int block_rows, int64_t x_rows) {
   using Q = QTile<T>;
-  // The tile keeps the input type (32 KB): row-major 16-byte writes, and the
+  // The tile keeps the input type (16 KB BF16, 32 KB fp32): row-major 16-byte writes, and the
   // column walks below read 32 consecutive columns per warp, so neither side
   // has shared-memory bank conflicts.
   __shared__ __align__(16) T tile[QBLOCK_ROWS][Q::COLS];
@@ -120,12 +122,12 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
   // Load: all eight 16-byte loads of a thread are issued before any is
   // written to shared memory, so 32 KB per CTA are in flight at once.
   {
-    const int cc = (tid & 15) * Q::VEC;
-    const int r_in = tid >> 4;
+    const int cc = (tid % Q::TPR) * Q::VEC;
+    const int r_in = tid / Q::TPR;
     uint4 buf[Q::ROW_PASSES];
 #pragma unroll
     for (int pass = 0; pass < Q::ROW_PASSES; ++pass) {
-      const int r = pass * 16 + r_in;
+      const int r = pass * Q::ROWS_PER_PASS + r_in;
       buf[pass] = make_uint4(0u, 0u, 0u, 0u);
       if (r < rows && cc < ncols) {
         int64_t xrow = gather_idx != nullptr ? static_cast<int64_t>(__ldg(gather_idx + row0 + r)) : row0 + r;
@@ -147,7 +149,7 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
     }
 #pragma unroll
     for (int pass = 0; pass < Q::ROW_PASSES; ++pass) {
-      *reinterpret_cast<uint4*>(&tile[pass * 16 + r_in][cc]) = buf[pass];
+      *reinterpret_cast<uint4*>(&tile[pass * Q::ROWS_PER_PASS + r_in][cc]) = buf[pass];
     }
   }
   __syncthreads();
