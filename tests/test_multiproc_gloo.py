@@ -105,3 +105,43 @@ def test_expert_sharded_wgrad_two_gloo_ranks(route):
         p.join(timeout=60)
         assert p.exitcode == 0
     assert results == {r: "ok" for r in range(world)}, results
+
+
+def _failing_worker(rank: int, world: int, port: int, q) -> None:
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    try:
+        if rank == 1:
+            raise RuntimeError("injected failure on rank 1")   # this rank never reaches the barrier
+        dist.barrier()                                           # the timing barrier of bench.py
+        q.put((rank, "ok"))
+    except Exception as exc:
+        q.put((rank, type(exc).__name__))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_failed_rank_is_detected_not_hung():
+    """A rank that fails before the timing barrier: the other rank's barrier ends
+    with an error after the process-group timeout instead of hanging, and the
+    parent sees both failures (host-side failure detection; no GPU involved)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        rank, status = q.get(timeout=120)
+        results[rank] = status
+    for p in procs:
+        p.join(timeout=60)
+    assert results[1] == "RuntimeError"
+    assert results[0] != "ok"
