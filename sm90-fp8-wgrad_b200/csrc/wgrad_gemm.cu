@@ -102,7 +102,7 @@ struct Cfg {
   static constexpr int OUT_STAGE_BYTES_PER_WARP = COLS_PER_WARP * 32 * 2 >= 8192 ? 8192 : 4096;
   static constexpr int TMEM_COLS = 2 * BN;          // double-buffered partial
   static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + EPI_WARPS * OUT_STAGE_BYTES_PER_WARP +
-                                    SCALE_STAGES * SCALE_FLOATS * 4 + 256 /*barriers*/ + 1024 /*align*/;
+                                    SCALE_STAGES * SCALE_FLOATS * 4 + 512 /*barriers*/ + 1024 /*align*/;
   static_assert(128 * REGS_CONTROL + 32 * EPI_WARPS * REGS_EPILOGUE <=
                     THREADS * ((65536 / (THREADS * CTAS_PER_SM)) & ~7),
                 "register split exceeds the launch allocation");
@@ -117,6 +117,13 @@ __device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, uint32_t (&r)[N]) 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -157,7 +164,8 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
   uint64_t* sempty_bar = sfull_bar + SCALE_STAGES;    // [SCALE_STAGES] epilogue -> TMA
   uint64_t* tfull_bar = sempty_bar + SCALE_STAGES;    // [2] MMA -> epilogue
   uint64_t* tempty_bar = tfull_bar + 2;               // [2] epilogue -> MMA
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  uint64_t* oldout_bar = tempty_bar + 2;             // [EPI_WARPS] previous output -> promotion warp (accumulate)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(oldout_bar + C::EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -181,6 +189,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
       mbar_init(&tfull_bar[i], 1);
       mbar_init(&tempty_bar[i], C::EPI_WARPS);
     }
+    for (int i = 0; i < C::EPI_WARPS; ++i) mbar_init(&oldout_bar[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -299,7 +308,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
     const uint32_t stage_out_addr = smem_u32(stage_out);
 
     int acc = 0, sstage = 0;
-    uint32_t aphase = 0, sphase = 0;
+    uint32_t aphase = 0, sphase = 0, oldout_phase = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
       const TileCoord tc = decode_tile(p, tile);
@@ -387,18 +396,6 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
         }
       }
 #endif
-      if (p.accumulate) {
-        const bool row_ok = g_row < p.m;
-        const size_t base = (static_cast<size_t>(tc.e) * p.m + (row_ok ? g_row : 0)) * p.n;
-#pragma unroll
-        for (int j = 0; j < C::COLS_PER_WARP; ++j) {
-          const int gc = col0 + j;
-          if (row_ok && gc < p.n) {
-            fin[j] += p.out_f32 ? reinterpret_cast<const float*>(p.out)[base + gc]
-                                : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.out)[base + gc]);
-          }
-        }
-      }
       // The previous tile's TMA store must have finished reading the staging buffer.
       WGRAD_PROF_T(ts1);
       if (lane == 0) bulk_wait_group_read0();
@@ -406,9 +403,46 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
       WGRAD_PROF_ADD(kProfEpiStoreWait, ts1);
       const bool rows_in = (tc.m0 + quarter * 32) < p.m;
       const uint32_t swz = static_cast<uint32_t>(lane & 7);
+      // accumulate: the previous output boxes come in through the same tensor
+      // map and 128B-swizzled staging layout the store uses (TMA load into this
+      // warp's staging area, bounded wait), so each thread adds its own row.
+      auto load_previous = [&](int nboxes, int box_cols, int first_box) -> bool {
+        if (lane == 0) {
+          uint32_t bytes = 0;
+          for (int b = 0; b < nboxes; ++b) bytes += col0 + (first_box + b) * box_cols < p.n ? 4096u : 0u;
+          mbar_arrive_expect_tx(&oldout_bar[ew], bytes);
+          for (int b = 0; b < nboxes; ++b) {
+            const int c = col0 + (first_box + b) * box_cols;
+            if (c < p.n) tma_load_3d(stage_out + b * 4096, &tmap_out, &oldout_bar[ew], c, tc.m0 + quarter * 32, tc.e);
+          }
+        }
+        const bool landed = mbar_wait(&oldout_bar[ew], oldout_phase, abort_flag, kDevTimeoutEpilogue);
+        oldout_phase ^= 1u;
+        return __all_sync(0xffffffffu, landed);
+      };
       if (!p.out_f32) {
         // bf16: boxes of 32 rows x 64 columns (128 B rows, 128B swizzle), 4 KB each.
         constexpr int BOXES = C::COLS_PER_WARP / 64;
+        if (p.accumulate && rows_in) {
+          ok = load_previous(BOXES, 64, 0);
+          if (!ok) break;
+#pragma unroll
+          for (int bx = 0; bx < BOXES; ++bx) {
+            const uint32_t box = stage_out_addr + bx * 4096 + lane * 128;
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+              const uint4 w = ld_shared_v4(box + ((ch ^ swz) << 4));
+              const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+              float* v = &fin[bx * 64 + ch * 8];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ww[i]));
+                v[2 * i] += f.x;
+                v[2 * i + 1] += f.y;
+              }
+            }
+          }
+        }
 #pragma unroll
         for (int bx = 0; bx < BOXES; ++bx) {
           const uint32_t box = stage_out_addr + bx * 4096 + lane * 128;
@@ -439,6 +473,23 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
             if (lane == 0) bulk_wait_group_read0();
             __syncwarp();
           }
+          if (p.accumulate && rows_in) {
+            ok = load_previous(PER_ROUND, 32, bx0);
+            if (!ok) break;
+#pragma unroll
+            for (int bi = 0; bi < PER_ROUND; ++bi) {
+              const uint32_t box = stage_out_addr + bi * 4096 + lane * 128;
+#pragma unroll
+              for (int ch = 0; ch < 8; ++ch) {
+                const uint4 w = ld_shared_v4(box + ((ch ^ swz) << 4));
+                float* v = &fin[(bx0 + bi) * 32 + ch * 4];
+                v[0] += __uint_as_float(w.x);
+                v[1] += __uint_as_float(w.y);
+                v[2] += __uint_as_float(w.z);
+                v[3] += __uint_as_float(w.w);
+              }
+            }
+          }
 #pragma unroll
           for (int bi = 0; bi < PER_ROUND; ++bi) {
             const uint32_t box = stage_out_addr + bi * 4096 + lane * 128;
@@ -461,6 +512,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
           }
         }
       }
+      if (!ok) break;
       WGRAD_PROF_ADD(kProfEpiStore, ts0);
     }
     if (lane == 0) bulk_wait_group0();  // all output writes complete before exit

@@ -238,3 +238,29 @@ def test_expert_range_launches_equal_full_launch(cuda_device, splits):
         assert torch.equal(part.view(torch.int16), full.view(torch.int16))
     with pytest.raises(RuntimeError, match="expert_range"):
         fp8_grouped_wgrad_sm90(ops[lk], ops[rk], full, meta, expert_range=(3, 2))
+
+
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta"])
+def test_accumulate_on_ragged_tiles(cuda_device, tuned_config, out_dtype):
+    """out += result where M, N are not multiples of the tile (the previous output
+    comes in through TMA boxes that reach past M and N) and experts are empty."""
+    from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
+
+    spec = {"counts": [0, 640, 3, 129, 0, 1100], "tokens": 700, "hidden": 272, "intermediate": 48, "seed": 9}
+    meta, _, ops = _gpu_case(spec, cuda_device)
+    om, oops = _oracle_case(spec)
+    for lk, rk in STAGES.values():
+        m, n = ops[lk].data.shape[1], ops[rk].data.shape[1]
+        ref = O.ref_scaled_wgrad(oops[lk], oops[rk], om)
+        gen = torch.Generator(device=cuda_device).manual_seed(3)
+        base = (torch.randn((6, m, n), device=cuda_device, generator=gen) * float(np.abs(ref).max())).to(out_dtype)
+        acc = base.clone()
+        fp8_grouped_wgrad_sm90(ops[lk], ops[rk], acc, meta, accumulate=True, tuned_config=tuned_config)
+        expect = base.float().cpu().numpy() + ref
+        if out_dtype == torch.bfloat16:
+            expect = O.bf16_round(expect)
+            np.testing.assert_allclose(acc.float().cpu().numpy(), expect, rtol=2 ** -7,
+                                       atol=1e-5 * float(np.abs(expect).max()))
+        else:
+            _check_f32(acc - base, ref)
