@@ -417,6 +417,14 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
           }
         }
         const bool landed = mbar_wait(&oldout_bar[ew], oldout_phase, abort_flag, kDevTimeoutEpilogue);
+        if (!landed) {
+          // Giving up (timeout, or another role aborted): let this warp's own
+          // load land before the CTA exits. Bounded, regardless of the abort flag.
+          const uint32_t addr = smem_u32(&oldout_bar[ew]);
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(addr, oldout_phase) && globaltimer_ns() - t0 < WGRAD_WAIT_TIMEOUT_NS) {
+          }
+        }
         oldout_phase ^= 1u;
         return __all_sync(0xffffffffu, landed);
       };
