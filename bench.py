@@ -216,6 +216,14 @@ def hbm_bytes_of(inp) -> float:
 
 
 # ---------------------------------------------------------------- CPU leg
+def _host_threads() -> int:
+    """Every host core this process may run on (affinity-aware)."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def cpu_reference_sample(workload: str, seed: int, target_s: float, max_experts: int | None = None) -> dict:
     """Time the reference's CPU algorithm (dequantise + fp32 matmul per 128-row
     block, checks.py:42-61; restated in oracle/) on a bounded sample of the
@@ -265,7 +273,7 @@ def run_reference(args) -> None:
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    torch.set_num_threads(os.cpu_count() or 1)
+    torch.set_num_threads(_host_threads())
     per_step = []
     sample = None
     for s in range(args.warmup + args.steps):
@@ -442,6 +450,7 @@ def run_ours(args) -> None:
         e2e = run_e2e(inp, args, world, dev, f_down + f_gate)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(_host_threads())   # after the GPU timing: all host cores for the CPU leg
         cpu = cpu_reference_sample(args.workload, args.seed, target_s=args.cpu_seconds)
         cpu.pop("seconds", None)
 
