@@ -20,11 +20,13 @@
 //                 TMEM partial buffers, then tcgen05.commit frees the smem
 //                 stage and signals the partial as ready.
 //   warps 2, 3  : idle (complete warpgroup 0, which gives registers away).
-//   warps 4..11 : promotion + epilogue. tcgen05.ld the partial (thread = TMEM
-//                 lane = output row), final += (raw * sb[n]) * sa[m] with packed
-//                 f32x2 FMA, release the TMEM buffer so the tensor pipe
-//                 computes block b+1 while block b is promoted. At tile end:
-//                 fp32 -> BF16 (or fp32), swizzled smem staging, TMA store.
+//   warps 4..    : promotion + epilogue (4, 8 or 16 warps, see Cfg). tcgen05.ld
+//                 the partial (thread = TMEM lane = output row), final +=
+//                 (raw * sb[n]) * sa[m] with packed f32x2 FMA, release the TMEM
+//                 buffer so the tensor pipe computes block b+1 while block b is
+//                 promoted. At tile end: fp32 -> BF16 (or fp32), swizzled smem
+//                 staging, TMA store (with accumulate, the previous output is
+//                 first TMA-loaded into the same staging area and added).
 // The serialised WGMMA -> wait -> promote chain of the SM90 kernel
 // (gemm_sm90.py:3945, 4023) becomes a two-deep TMEM pipeline here.
 //
