@@ -405,6 +405,7 @@ def run_ours(args) -> None:
     clk = clocks.stop()
     _barrier(world, dev)
     total_ms = evs[0][0].elapsed_time(evs[-1][2])
+    step_ms = sorted(e[0].elapsed_time(e[2]) for e in evs)   # per-step spread (timing.py: mean/min/p90)
     down_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
     gate_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
     local_ms = total_ms / args.steps
@@ -479,6 +480,8 @@ def run_ours(args) -> None:
             "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "ms_per_step_min": step_ms[0],
+            "ms_per_step_p90": step_ms[min(len(step_ms) - 1, int(round(0.9 * (len(step_ms) - 1))))],
             "clocks": clk,
             "check": check,
             "gpu_launches": 2 * args.steps,
