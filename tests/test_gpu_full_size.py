@@ -84,3 +84,65 @@ def test_full_size_sampled_experts(cuda_device, name, layout):
             assert cd <= 1e-5, (name, layout, e, counts[e], cd)
     for e in empty:
         assert not inp.down_out_bf16[e].any() and not inp.gate_up_out_bf16[e].any(), (name, e)
+
+
+@pytest.mark.parametrize("policy", ["adaptive64", "adaptive32_64_twophase"])
+def test_full_size_packed_tail_policies(cuda_device, monkeypatch, policy):
+    """Packed layout with the adaptive tail-copy policies at full size (their
+    kernel_data offsets and guard rows differ from masked128): every sampled
+    expert of the skewed DeepSeek-V3 32k problem within the gate."""
+    from sm90_fp8_wgrad.layout_mode import PACKED_TAIL_ENV
+    from sm90_fp8_wgrad.matrix import check_sampled_experts
+    from sm90_fp8_wgrad.routing import make_routing
+    from sm90_fp8_wgrad.synthetic import make_synthetic_wgrad_inputs, run_custom_down, run_custom_gate_up
+
+    monkeypatch.setenv(PACKED_TAIL_ENV, policy)
+    experts, top_k, hidden, inter, tokens, route, _ = CONFIGS["dsv3_skewed_32k"]
+    routing = make_routing(tokens=tokens, experts=experts, top_k=top_k, route=route, seed=1234)
+    inp = make_synthetic_wgrad_inputs(tokens=tokens, experts=experts, top_k=top_k, hidden=hidden,
+                                      intermediate=inter, route=route, seed=1234, device=cuda_device,
+                                      routing=routing, layout_mode="packed")
+    assert inp.meta.packed_tail_tma_mode == policy
+    inp.drop_sources()
+    run_custom_down(inp)
+    run_custom_gate_up(inp)
+    torch.cuda.synchronize()
+    diff, zeros_ok, rel = check_sampled_experts(inp, "packed", with_rel_err=True)
+    assert zeros_ok and diff <= 1e-5, (policy, diff, rel)
+
+
+def test_full_size_accumulate_and_expert_ranges(cuda_device):
+    """DeepSeek-V3 32k down GEMM: 16 expert-range launches equal one launch bit for
+    bit, and accumulate=True into fp32 adds exactly the launch's result to the
+    previous contents (sampled experts vs the fp32 reference)."""
+    from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
+    from sm90_fp8_wgrad.routing import make_routing
+    from sm90_fp8_wgrad.synthetic import make_synthetic_wgrad_inputs
+
+    experts, top_k, hidden, inter, tokens, route, _ = CONFIGS["dsv3_32k"]
+    routing = make_routing(tokens=tokens, experts=experts, top_k=top_k, route=route, seed=1234)
+    inp = make_synthetic_wgrad_inputs(tokens=tokens, experts=experts, top_k=top_k, hidden=hidden,
+                                      intermediate=inter, route=route, seed=1234, device=cuda_device,
+                                      routing=routing)
+    inp.drop_sources()
+    lhs, rhs, meta = inp.grad_y_q, inp.hidden_q, inp.meta
+    full = torch.empty_like(inp.down_out_bf16)
+    fp8_grouped_wgrad_sm90(lhs, rhs, full, meta)
+    part = torch.empty_like(full)
+    for c in range(16):
+        fp8_grouped_wgrad_sm90(lhs, rhs, part, meta, expert_range=(c * experts // 16, (c + 1) * experts // 16))
+    torch.cuda.synchronize()
+    assert torch.equal(part.view(torch.int16), full.view(torch.int16))
+
+    base = torch.full(full.shape, 0.25, device=cuda_device, dtype=torch.float32)
+    fp8_grouped_wgrad_sm90(lhs, rhs, base, meta, accumulate=True)
+    torch.cuda.synchronize()
+    base -= 0.25                      # the accumulated result minus the initial value
+    counts = inp.counts
+    nonempty = [e for e, c in enumerate(counts) if c > 0]
+    cu = meta.padded_cu_seqlens_k.cpu().tolist()
+    bo = meta.block_offsets.cpu().tolist()
+    for e in (max(nonempty, key=lambda x: counts[x]), min(nonempty, key=lambda x: counts[x])):
+        k0, k1, b0 = cu[e], cu[e + 1], bo[e]
+        ref = _dequant(lhs, k0, k1, b0).t() @ _dequant(rhs, k0, k1, b0)
+        assert _calc_diff(base[e], ref) <= 1e-5
