@@ -264,3 +264,31 @@ def test_accumulate_on_ragged_tiles(cuda_device, tuned_config, out_dtype):
                                        atol=1e-5 * float(np.abs(expect).max()))
         else:
             _check_f32(acc - base, ref)
+
+
+def test_legacy_quantiser_entry_point(cuda_device):
+    """sm100_wgrad_quantize_1x128 (the plain C entry, padded layout) called through
+    ctypes the way a C-ABI user would: bytes and scales bit-exact to the oracle."""
+    import ctypes
+
+    from sm90_fp8_wgrad import _lib, build_wgrad_scale_block_meta
+
+    spec = SMALL_CASES["mixed"]
+    meta = build_wgrad_scale_block_meta(torch.from_numpy(_cu(spec["counts"])).to(cuda_device, torch.int32))
+    om, oops = _oracle_case(spec)
+    inp = case_inputs(spec)
+    lib = _lib.load()
+    for k, v in inp.items():
+        x = torch.from_numpy(v).to(cuda_device).to(torch.bfloat16).contiguous()
+        rows, cols = x.shape
+        pitch = max(128, (int(meta.padded_rows) + 127) // 128 * 128)
+        q = torch.zeros((cols, pitch), device=cuda_device, dtype=torch.uint8)
+        scales = torch.empty((int(meta.total_blocks), cols), device=cuda_device, dtype=torch.float32)
+        st = lib.sm100_wgrad_quantize_1x128(
+            ctypes.c_void_p(x.data_ptr()), 0, rows, cols, ctypes.c_void_p(meta.block_row_start.data_ptr()),
+            ctypes.c_void_p(meta.block_row_count.data_ptr()), int(meta.total_blocks), ctypes.c_void_p(q.data_ptr()),
+            pitch, ctypes.c_void_p(scales.data_ptr()), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert st == _lib.OK, st
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(q[:, : om.padded_rows].cpu().numpy(), oops[k].data[:, : om.padded_rows], err_msg=k)
+        np.testing.assert_array_equal(scales.cpu().numpy().view(np.uint32), oops[k].scales.view(np.uint32), err_msg=k)
