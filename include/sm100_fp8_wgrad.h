@@ -63,6 +63,7 @@ extern "C" {
 #define SM100_WGRAD_TILE_128x256_W8 3
 #define SM100_WGRAD_TILE_128x256_W16 4
 #define SM100_WGRAD_TILE_128x128_2CTA 5   /* 128x128 tile, two CTAs (pipelines) per SM */
+#define SM100_WGRAD_TILE_128x192_W12 6    /* 128x192 tile, 12 promotion warps          */
 
 typedef struct Sm100WgradArgs {
   const void* lhs_data;      /* FP8 e4m3 [M][lhs_pitch]                              */

@@ -114,6 +114,7 @@ int encode_out_map(CUtensorMap* map, void* out, int out_f32, int64_t e, int64_t 
 
 int pick_bn(int32_t tile_config, int64_t n) {
   if (tile_config == SM100_WGRAD_TILE_128x128 || tile_config == SM100_WGRAD_TILE_128x128_2CTA) return 128;
+  if (tile_config == SM100_WGRAD_TILE_128x192_W12) return 192;
   if (tile_config == SM100_WGRAD_TILE_128x256 || tile_config == SM100_WGRAD_TILE_128x256_W8 ||
       tile_config == SM100_WGRAD_TILE_128x256_W16)
     return 256;
@@ -129,6 +130,7 @@ constexpr int64_t kShortKBlocksPerExpert = 2;
 
 int pick_epi_warps(int32_t tile_config, int bn, int64_t total_blocks, int64_t num_experts) {
   if (tile_config == SM100_WGRAD_TILE_128x128_2CTA) return 4;
+  if (tile_config == SM100_WGRAD_TILE_128x192_W12) return 12;
   if (bn != 256 || tile_config == SM100_WGRAD_TILE_128x256_W8) return 8;
   if (tile_config == SM100_WGRAD_TILE_128x256_W16) return 16;
   return total_blocks <= kShortKBlocksPerExpert * num_experts ? 16 : 8;
@@ -159,7 +161,7 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   if (a->num_experts < 0 || a->m <= 0 || a->n <= 0 || a->k_rows < 0 || a->total_blocks < 0)
     return SM100_WGRAD_ERR_INVALID_ARG;
   if (a->out_dtype != SM100_WGRAD_OUT_BF16 && a->out_dtype != SM100_WGRAD_OUT_F32) return SM100_WGRAD_ERR_INVALID_ARG;
-  if (a->tile_config < SM100_WGRAD_TILE_AUTO || a->tile_config > SM100_WGRAD_TILE_128x128_2CTA)
+  if (a->tile_config < SM100_WGRAD_TILE_AUTO || a->tile_config > SM100_WGRAD_TILE_128x192_W12)
     return SM100_WGRAD_ERR_INVALID_ARG;
   // TMA: output row pitch and scale-vector chunks must be 16-byte multiples.
   if (a->m % 16 != 0 || a->n % 16 != 0) return SM100_WGRAD_ERR_UNSUPPORTED;

@@ -79,6 +79,7 @@ constexpr int FIRST_EPI_WARP = 4;
 // each owns 32 rows x BN / (EPI / 4) columns. 16 warps keep more TMEM loads,
 // scale loads and output stores in flight (better for short-K, HBM-bound
 // launches); 8 warps carry fewer per-warp fixed costs (better for long K).
+// EPI = 12 (with BN = 192) puts three 64-column warps on each sub-partition.
 // EPI = 4 (with BN = 128) runs two CTAs per SM: two independent pipelines on
 // different tiles whose promotion warps share each SM sub-partition, so the
 // stalls of one fill the FMA pipe with the other's work.
@@ -93,16 +94,19 @@ struct Cfg {
   static constexpr int THREADS = 32 * (4 + EPI_WARPS);
   static constexpr int CTAS_PER_SM = EPI_WARPS == 4 ? 2 : 1;
   static constexpr int STAGES = EPI_WARPS == 4 ? 2 : 3;
-  static constexpr uint32_t REGS_CONTROL = EPI_WARPS == 16 ? 32 : 56;
-  static constexpr uint32_t REGS_EPILOGUE = EPI_WARPS == 16 ? 112 : (EPI_WARPS == 4 ? 200 : 224);
+  static constexpr uint32_t REGS_CONTROL = EPI_WARPS == 16 ? 32 : (EPI_WARPS == 12 ? 40 : 56);
+  static constexpr uint32_t REGS_EPILOGUE =
+      EPI_WARPS == 16 ? 112 : (EPI_WARPS == 12 ? 152 : (EPI_WARPS == 4 ? 200 : 224));
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int SCALE_FLOATS = BM + BN;
   static constexpr int COLS_PER_WARP = BN / (EPI_WARPS / 4);  // EPI_WARPS / 4 column groups
-  static constexpr int CHUNK = COLS_PER_WARP >= 128 && REGS_EPILOGUE >= 224 ? 32 : 16;  // tcgen05.ld columns
+  // tcgen05.ld columns per load: 32 when two such buffers fit beside the accumulator
+  static constexpr int CHUNK = REGS_EPILOGUE >= COLS_PER_WARP + 80 ? 32 : 16;
   static constexpr int CHUNKS = COLS_PER_WARP / CHUNK;
   static constexpr int OUT_STAGE_BYTES_PER_WARP = COLS_PER_WARP * 32 * 2 >= 8192 ? 8192 : 4096;
-  static constexpr int TMEM_COLS = 2 * BN;          // double-buffered partial
+  // double-buffered partial, allocated as a power of two (192-wide tiles use 384 of 512)
+  static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
   static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + EPI_WARPS * OUT_STAGE_BYTES_PER_WARP +
                                     SCALE_STAGES * SCALE_FLOATS * 4 + 512 /*barriers*/ + 1024 /*align*/;
   static_assert(128 * REGS_CONTROL + 32 * EPI_WARPS * REGS_EPILOGUE <=
@@ -566,6 +570,7 @@ cudaError_t launch_grouped_wgrad(const CUtensorMap& ta, const CUtensorMap& tb, c
     return p.epi_warps == 16 ? launch_impl<256, 16>(ta, tb, to, p, grid, stream)
                              : launch_impl<256, 8>(ta, tb, to, p, grid, stream);
   }
+  if (p.bn == 192) return launch_impl<192, 12>(ta, tb, to, p, grid, stream);
   return p.epi_warps == 4 ? launch_impl<128, 4>(ta, tb, to, p, grid, stream)
                           : launch_impl<128, 8>(ta, tb, to, p, grid, stream);
 }

@@ -33,6 +33,7 @@ TILE_128x128 = 2
 TILE_128x256_W8 = 3
 TILE_128x256_W16 = 4
 TILE_128x128_2CTA = 5
+TILE_128x192_W12 = 6
 
 # Every symbol include/sm100_fp8_wgrad.h declares.
 EXPORTED_SYMBOLS = (

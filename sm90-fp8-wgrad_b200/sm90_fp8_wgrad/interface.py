@@ -62,6 +62,7 @@ TUNED_CONFIGS: dict[str, int] = {
     "sm100_128x256_w8": _lib.TILE_128x256_W8,     # 8 promotion warps
     "sm100_128x256_w16": _lib.TILE_128x256_W16,   # 16 promotion warps
     "sm100_128x128_2cta": _lib.TILE_128x128_2CTA,  # two 128x128 pipelines (CTAs) per SM
+    "sm100_128x192_w12": _lib.TILE_128x192_W12,    # 192-column tile, 12 promotion warps
 }
 
 

@@ -138,7 +138,7 @@ def test_quantiser_fp32_input_and_odd_columns(cuda_device):
     np.testing.assert_array_equal(op.scales.cpu().numpy().view(np.uint32), ref.scales.view(np.uint32))
 
 
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x128", "sm100_128x256_w8", "sm100_128x256_w16", "sm100_128x128_2cta"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x128", "sm100_128x256_w8", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_128x192_w12"])
 @pytest.mark.parametrize("case", sorted(SMALL_CASES) + ["c1"])
 def test_grouped_wgrad_matches_oracle(cuda_device, case, tuned_config):
     from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
@@ -159,7 +159,7 @@ def test_grouped_wgrad_matches_oracle(cuda_device, case, tuned_config):
     assert _lib.device_error() == 0
 
 
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w8", "sm100_128x256_w16", "sm100_128x128_2cta"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w8", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_128x192_w12"])
 def test_grouped_wgrad_fp32_out_and_accumulate(cuda_device, tuned_config):
     from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
 
@@ -185,7 +185,7 @@ def test_grouped_wgrad_fp32_out_and_accumulate(cuda_device, tuned_config):
     np.testing.assert_allclose(got, expect, rtol=2 ** -7, atol=1e-5 * float(np.abs(expect).max()))
 
 
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_128x192_w12"])
 @pytest.mark.parametrize("hidden,inter", [(144, 80), (272, 48), (512, 128)])
 def test_grouped_wgrad_ragged_tiles(cuda_device, hidden, inter, tuned_config):
     """M, N not multiples of the 128 x 256 tile; empty experts; long K."""
@@ -241,7 +241,7 @@ def test_expert_range_launches_equal_full_launch(cuda_device, splits):
 
 
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_128x192_w12"])
 def test_accumulate_on_ragged_tiles(cuda_device, tuned_config, out_dtype):
     """out += result where M, N are not multiples of the tile (the previous output
     comes in through TMA boxes that reach past M and N) and experts are empty."""
