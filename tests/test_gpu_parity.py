@@ -292,3 +292,22 @@ def test_legacy_quantiser_entry_point(cuda_device):
         torch.cuda.synchronize()
         np.testing.assert_array_equal(q[:, : om.padded_rows].cpu().numpy(), oops[k].data[:, : om.padded_rows], err_msg=k)
         np.testing.assert_array_equal(scales.cpu().numpy().view(np.uint32), oops[k].scales.view(np.uint32), err_msg=k)
+
+
+@pytest.mark.parametrize("counts", [[0, 0, 0, 0], [300], [(e * 7) % 4 for e in range(1024)]],
+                         ids=["all_empty", "one_expert", "1024_tiny_experts"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta"])
+def test_grouped_wgrad_edge_expert_sets(cuda_device, counts, tuned_config):
+    """Every expert empty (no K rows at all: the launch has no operands and writes
+    zeros), a single expert, and 1,024 experts of 0-3 rows each."""
+    from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
+
+    spec = {"counts": counts, "tokens": max(8, sum(counts)), "hidden": 144, "intermediate": 80, "seed": 13}
+    meta, _, ops = _gpu_case(spec, cuda_device)
+    om, oops = _oracle_case(spec)
+    e = len(counts)
+    for lk, rk in STAGES.values():
+        m, n = ops[lk].data.shape[1], ops[rk].data.shape[1]
+        out = torch.full((e, m, n), float("nan"), device=cuda_device, dtype=torch.bfloat16)
+        fp8_grouped_wgrad_sm90(ops[lk], ops[rk], out, meta, tuned_config=tuned_config)
+        _check_bf16(out, O.ref_scaled_wgrad(oops[lk], oops[rk], om))
