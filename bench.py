@@ -307,10 +307,11 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def workload_config(workload: str, world: int, layout: str = "padded") -> dict:
+def workload_config(workload: str, world: int, layout: str = "padded", scale_format: str = "fp32") -> dict:
     e_all, top_k, h, i, t, route = WORKLOADS[workload]
     return {"workload": workload, "experts": e_all, "top_k": top_k, "hidden": h, "intermediate": i,
             "tokens": t, "route": route, "parallelism": f"ep{world}", "layout": layout,
+            "scale_format": scale_format,
             "l2": "inputs larger than L2 (no flush needed)" if workload not in ("tiny",) else "flush"}
 
 
@@ -372,7 +373,7 @@ def run_ours(args) -> None:
     t_setup = time.perf_counter()
     inp = make_synthetic_wgrad_inputs(tokens=t, experts=e_all, top_k=top_k, hidden=h, intermediate=i, route=route,
                                       seed=args.seed, device=dev, expert_range=(e0, e1), routing=routing,
-                                      layout_mode=args.layout)
+                                      layout_mode=args.layout, scale_format=args.scale_format)
     inp.drop_sources()
     torch.cuda.empty_cache()
     torch.cuda.synchronize(dev)
@@ -426,8 +427,10 @@ def run_ours(args) -> None:
     bound = "tensor" if t_tc >= t_hbm else "hbm"
     gate_flops_tf = f_gate / (gate_ms * 1e-3) / 1e12
     down_flops_tf = f_down / (down_ms * 1e-3) / 1e12
+    kname = ("grouped_wgrad_ue8m0_kernel (gate_up launch)" if args.scale_format == "ue8m0"
+             else "grouped_wgrad_kernel<256> (gate_up launch)")
     if bound == "tensor":
-        roof = {"bound": "tensor", "kernel": "grouped_wgrad_kernel<256> (gate_up launch)",
+        roof = {"bound": "tensor", "kernel": kname,
                 "achieved": gate_flops_tf, "peak": fp8_peak, "unit": "TFLOP/s", "frac": gate_flops_tf / fp8_peak,
                 "peak_source": "2 x measured bf16 cuBLAS burst (MEASURED_PEAKS.json)"
                                + (" fallback" if peaks.get("_fallback") else ""),
@@ -435,10 +438,11 @@ def run_ours(args) -> None:
     else:
         gate_bytes = step_bytes * 2.0 / 3.0
         gbs = gate_bytes / (gate_ms * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": "grouped_wgrad_kernel<256> (gate_up launch)", "achieved": gbs,
+        roof = {"bound": "hbm", "kernel": kname, "achieved": gbs,
                 "peak": float(peaks["hbm_gbs"]), "unit": "GB/s", "frac": gbs / float(peaks["hbm_gbs"]),
                 "peak_source": "measured copy bandwidth (MEASURED_PEAKS.json)"}
-    traffic = _profile_traffic(args.workload)
+    # The committed capture is of the promotion kernel on fp32 scales.
+    traffic = _profile_traffic(args.workload) if args.scale_format == "fp32" else None
     # The ncu capture is of the 1-GPU launch; a rank's launch moves its experts' share.
     roof["traffic"] = None if traffic is None else float(traffic) * (e1 - e0) / e_all
     roof["traffic_unit"] = ("DRAM bytes per gate_up launch (ncu, profiles/grouped_wgrad_kernel_dsv3_32k_launches.md"
@@ -468,10 +472,10 @@ def run_ours(args) -> None:
             "scaling": "strong",
             "vs_baseline": (value / H100_REFERENCE_TFLOPS[args.workload]) if (
                 world == 1 and args.workload in H100_REFERENCE_TFLOPS) else None,
-            "vs_baseline_ref": "reference sm90 kernel on H100, same per-GPU problem (BASELINE.md)",
+            "vs_baseline_ref": "published reference sm90 kernel figure on H100, same per-GPU problem",
             "dtype": "fp8e4m3->f32acc->bf16",
             "data": "synthetic",
-            "config": workload_config(args.workload, world, args.layout),
+            "config": workload_config(args.workload, world, args.layout, args.scale_format),
             "stages_ms": {"down": down_ms, "gate_up": gate_ms},
             "stages_tflops": {"down": down_flops_tf, "gate_up": gate_flops_tf},
             "pct_of_fp8_peak": value / world / fp8_peak,
@@ -601,6 +605,9 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--layout", choices=("padded", "packed"), default="padded",
                     help="operand layout (KERNEL_LAB_WGRAD_LAYOUT_MODE of the reference)")
+    ap.add_argument("--scale-format", choices=("fp32", "ue8m0"), default="fp32",
+                    help="fp32: the reference's amax/448 scales (default, the headline); ue8m0: scales "
+                         "rounded up to powers of two, applied by the block-scaled kernel")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")

@@ -64,6 +64,12 @@ extern "C" {
 #define SM100_WGRAD_TILE_128x256_W16 4
 #define SM100_WGRAD_TILE_128x128_2CTA 5   /* 128x128 tile, two CTAs (pipelines) per SM */
 #define SM100_WGRAD_TILE_128x192_W12 6    /* 128x192 tile, 12 promotion warps          */
+/* 128x192 tile for UE8M0 scales: every scale must be a positive power of two
+ * (the quantiser's scale_format 1); the tensor core applies them as E8M0 block
+ * scales (tcgen05.mma kind::mxf8f6f4.block_scale) and no fp32 promotion runs.
+ * A scale with mantissa bits set is taken as 1.0 and sets device error 6.
+ * Never chosen by AUTO. */
+#define SM100_WGRAD_TILE_128x192_UE8M0 7
 
 typedef struct Sm100WgradArgs {
   const void* lhs_data;      /* FP8 e4m3 [M][lhs_pitch]                              */
@@ -159,6 +165,9 @@ typedef struct Sm100WgradQuantArgs {
                                      the compact tail operands of quant.py:273-307        */
   int64_t x_rows;                 /* rows of x; required with gather_idx (an index outside
                                      [0, x_rows) reads zeros and sets device error 5)      */
+  int32_t scale_format;           /* 0: fp32 scale max(amax / 448, 1e-12) as the reference;
+                                     1: that scale rounded up to a power of two (UE8M0, for
+                                     SM100_WGRAD_TILE_128x192_UE8M0)                       */
 } Sm100WgradQuantArgs;
 
 SM100_WGRAD_API int sm100_wgrad_quantize_1x128_ex(const Sm100WgradQuantArgs* args, void* stream);

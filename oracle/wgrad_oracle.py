@@ -186,11 +186,24 @@ class OracleOperand:
         return e4m3_decode(self.data[:, b * BLOCK_K : b * BLOCK_K + rows]).T
 
 
-def quantize_blocks(x: np.ndarray, block_row_start, block_row_count, block_k: int, padded_rows: int) -> OracleOperand:
+def round_up_pow2(scale: np.ndarray) -> np.ndarray:
+    """UE8M0 scale (an extension with no counterpart in the reference): the
+    smallest power of two >= the positive fp32 scale, by its bit pattern -- a
+    set mantissa bit moves the value to the next exponent; inf / NaN stay."""
+    bits = np.asarray(scale, dtype=np.float32).view(np.uint32)
+    special = (bits & np.uint32(0x7F800000)) == np.uint32(0x7F800000)
+    exact = (bits & np.uint32(0x7FFFFF)) == 0
+    up = (bits & np.uint32(0xFF800000)) + np.uint32(0x800000)
+    return np.where(special | exact, bits, up).astype(np.uint32).view(np.float32)
+
+
+def quantize_blocks(x: np.ndarray, block_row_start, block_row_count, block_k: int, padded_rows: int,
+                    scale_format: str = "fp32") -> OracleOperand:
     """quant.py:129-167 for any scale-block height (the kernel's BLOCK_K is
     meta.block_k, quant.py:258): block b's valid rows are quantised with
     per-column amax/448 scales into padded rows block_k * b + k (quant.py:139),
-    pitch = max(128, ceil(K/128)*128) and padded rows zero (quant.py:222-247)."""
+    pitch = max(128, ceil(K/128)*128) and padded rows zero (quant.py:222-247).
+    ``scale_format="ue8m0"`` rounds each scale up to a power of two first."""
     x = np.asarray(x, dtype=np.float32)
     cols = x.shape[1]
     nblocks = len(block_row_start)
@@ -202,18 +215,20 @@ def quantize_blocks(x: np.ndarray, block_row_start, block_row_count, block_k: in
         blk = x[r0 : r0 + n]                                         # valid rows only (mask k < row_count)
         amax = np.abs(blk).max(axis=0) if n else np.zeros(cols, np.float32)
         scale = np.maximum((amax / FP8_MAX).astype(np.float32), SCALE_EPS)  # fp32 division, eps floor
+        if scale_format == "ue8m0":
+            scale = round_up_pow2(scale)
         scales[b] = scale
         q = (blk / scale[None, :]).astype(np.float32)                # x / scale, fp32
         data[:, b * block_k : b * block_k + n] = e4m3_encode(q).T
     return OracleOperand(data=data, scales=scales, k_rows=padded_rows)
 
 
-def quantize_1x128(x: np.ndarray, meta: OracleMeta) -> OracleOperand:
+def quantize_1x128(x: np.ndarray, meta: OracleMeta, scale_format: str = "fp32") -> OracleOperand:
     """The padded 128-row operand (quant.py:129-167, :222-247)."""
     x = np.asarray(x, dtype=np.float32)
     if x.ndim != 2 or x.shape[0] != meta.valid_rows:
         raise RuntimeError("x must be [valid_rows, cols]")
-    return quantize_blocks(x, meta.block_row_start, meta.block_row_count, BLOCK_K, meta.padded_rows)
+    return quantize_blocks(x, meta.block_row_start, meta.block_row_count, BLOCK_K, meta.padded_rows, scale_format)
 
 
 _PACKED_GUARD_ROWS = {"masked128": 127, "adaptive64": 63, "adaptive32_64_128": 127, "adaptive32_64_twophase": 31}

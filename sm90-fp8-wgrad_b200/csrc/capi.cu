@@ -19,7 +19,7 @@ cudaError_t launch_quantize_1x128(const void* x, int x_dtype, int64_t cols, cons
                                   const int32_t* block_row_start, const int32_t* block_row_count,
                                   int64_t total_blocks, void* q, int64_t q_pitch, const int32_t* q_row_start,
                                   bool q_zero_fill, void* kq, int64_t kq_pitch, const int32_t* kq_row_start,
-                                  float* scales, int block_rows, int64_t x_rows, cudaStream_t stream);
+                                  float* scales, int block_rows, int64_t x_rows, bool ue8m0, cudaStream_t stream);
 cudaError_t launch_build_meta(const int32_t* cu, int64_t num_experts, const Sm100WgradMetaOut& out,
                               cudaStream_t stream);
 }  // namespace wgrad
@@ -114,7 +114,7 @@ int encode_out_map(CUtensorMap* map, void* out, int out_f32, int64_t e, int64_t 
 
 int pick_bn(int32_t tile_config, int64_t n) {
   if (tile_config == SM100_WGRAD_TILE_128x128 || tile_config == SM100_WGRAD_TILE_128x128_2CTA) return 128;
-  if (tile_config == SM100_WGRAD_TILE_128x192_W12) return 192;
+  if (tile_config == SM100_WGRAD_TILE_128x192_W12 || tile_config == SM100_WGRAD_TILE_128x192_UE8M0) return 192;
   if (tile_config == SM100_WGRAD_TILE_128x256 || tile_config == SM100_WGRAD_TILE_128x256_W8 ||
       tile_config == SM100_WGRAD_TILE_128x256_W16)
     return 256;
@@ -130,7 +130,7 @@ constexpr int64_t kShortKBlocksPerExpert = 2;
 
 int pick_epi_warps(int32_t tile_config, int bn, int64_t total_blocks, int64_t num_experts) {
   if (tile_config == SM100_WGRAD_TILE_128x128_2CTA) return 4;
-  if (tile_config == SM100_WGRAD_TILE_128x192_W12) return 12;
+  if (tile_config == SM100_WGRAD_TILE_128x192_W12 || tile_config == SM100_WGRAD_TILE_128x192_UE8M0) return 12;
   if (bn != 256 || tile_config == SM100_WGRAD_TILE_128x256_W8) return 8;
   if (tile_config == SM100_WGRAD_TILE_128x256_W16) return 16;
   return total_blocks <= kShortKBlocksPerExpert * num_experts ? 16 : 8;
@@ -161,7 +161,7 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   if (a->num_experts < 0 || a->m <= 0 || a->n <= 0 || a->k_rows < 0 || a->total_blocks < 0)
     return SM100_WGRAD_ERR_INVALID_ARG;
   if (a->out_dtype != SM100_WGRAD_OUT_BF16 && a->out_dtype != SM100_WGRAD_OUT_F32) return SM100_WGRAD_ERR_INVALID_ARG;
-  if (a->tile_config < SM100_WGRAD_TILE_AUTO || a->tile_config > SM100_WGRAD_TILE_128x192_W12)
+  if (a->tile_config < SM100_WGRAD_TILE_AUTO || a->tile_config > SM100_WGRAD_TILE_128x192_UE8M0)
     return SM100_WGRAD_ERR_INVALID_ARG;
   // TMA: output row pitch and scale-vector chunks must be 16-byte multiples.
   if (a->m % 16 != 0 || a->n % 16 != 0) return SM100_WGRAD_ERR_UNSUPPORTED;
@@ -228,6 +228,9 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
     else return SM100_WGRAD_ERR_INVALID_ARG;
     if (!WGRAD_DEBUG_MODES) return SM100_WGRAD_ERR_UNSUPPORTED;
   }
+  p.ue8m0 = a->tile_config == SM100_WGRAD_TILE_128x192_UE8M0 ? 1 : 0;
+  // The known-answer modes instrument the promotion loop, which the UE8M0 kernel does not have.
+  if (p.ue8m0 && p.mode != wgrad::kModeNormal) return SM100_WGRAD_ERR_UNSUPPORTED;
   // Test-only failure injection of the bounded-wait path (never set in normal use).
   const char* inject = std::getenv("SM100_WGRAD_DEBUG_INJECT");
   p.inject = (inject != nullptr && std::strcmp(inject, "withhold_first_load") == 0) ? wgrad::kInjectWithholdFirstLoad : 0;
@@ -255,7 +258,8 @@ int sm100_wgrad_quantize_1x128(const void* x, int32_t x_dtype, int64_t valid_row
   if (st != SM100_WGRAD_OK) return st;
   const cudaError_t err = wgrad::launch_quantize_1x128(x, x_dtype, cols, nullptr, block_row_start, block_row_count,
                                                        total_blocks, q_data, q_pitch, nullptr, true, nullptr, 0,
-                                                       nullptr, scales, 128, valid_rows, static_cast<cudaStream_t>(stream));
+                                                       nullptr, scales, 128, valid_rows, false,
+                                                       static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? SM100_WGRAD_OK : SM100_WGRAD_ERR_LAUNCH;
 }
 
@@ -273,6 +277,7 @@ int sm100_wgrad_quantize_1x128_ex(const Sm100WgradQuantArgs* a, void* stream) {
   if (a->q_row_start == nullptr && (a->q_pitch < a->total_blocks * block_rows || a->q_pitch % 16 != 0))
     return SM100_WGRAD_ERR_INVALID_ARG;
   if (a->kq_data != nullptr && a->kq_row_start == nullptr) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->scale_format != 0 && a->scale_format != 1) return SM100_WGRAD_ERR_INVALID_ARG;
   if (a->total_blocks > INT32_MAX) return SM100_WGRAD_ERR_UNSUPPORTED;
   DeviceInfo info;
   const int st = check_arch(&info);
@@ -280,7 +285,7 @@ int sm100_wgrad_quantize_1x128_ex(const Sm100WgradQuantArgs* a, void* stream) {
   const cudaError_t err = wgrad::launch_quantize_1x128(
       a->x, a->x_dtype, a->cols, a->gather_idx, a->block_row_start, a->block_row_count, a->total_blocks, a->q_data,
       a->q_pitch, a->q_row_start, a->q_zero_fill != 0, a->kq_data, a->kq_pitch, a->kq_row_start, a->scales,
-      block_rows, a->x_rows, static_cast<cudaStream_t>(stream));
+      block_rows, a->x_rows, a->scale_format == 1, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? SM100_WGRAD_OK : SM100_WGRAD_ERR_LAUNCH;
 }
 

@@ -25,6 +25,7 @@ enum DeviceError : unsigned int {
   kDevTimeoutEpilogue = 3,
   kDevBadTile = 4,
   kDevBadGatherIndex = 5,  // quantiser gather index outside [0, x_rows)
+  kDevScaleNotPow2 = 6,    // UE8M0 GEMM given a scale that is not a positive power of two
 };
 
 // Module-global device error word (read and cleared by sm100_wgrad_device_error).
@@ -200,6 +201,19 @@ __device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t a_desc, uint64
       : "memory");
 }
 
+// D[tmem] (+)= (A * 2^sfa) * (B * 2^sfb)^T, FP8 x FP8 -> FP32 with UE8M0 block
+// scales read from TMEM (one scale per row of A / B per 32-wide K slice,
+// scale_vec::1X), issued by one thread.
+__device__ __forceinline__ void umma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
 // Arrive once on an mbarrier when all prior tcgen05 async ops of this thread complete.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -244,6 +258,23 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
       : "memory");
 }
 
+// 32 lanes x N consecutive 32-bit columns from registers: thread i writes lane
+// (taddr.lane + i), columns [taddr.col, taddr.col + N).
+__device__ __forceinline__ void tmem_st_32x32b_x4(uint32_t taddr, uint32_t v0, uint32_t v1, uint32_t v2,
+                                                  uint32_t v3) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v0), "r"(v1),
+               "r"(v2), "r"(v3)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA
 // with 128-byte swizzling: rows of 128 bytes, 8-row core groups 1024 bytes
 // apart. Bit layout: start>>4 [0,14), LBO>>4 [16,30), SBO>>4 [32,46),
@@ -263,6 +294,16 @@ __host__ __device__ constexpr uint32_t umma_idesc_e4m3_f32(int m, int n) {
   return (1u << 4)                                  // D format F32
          | (0u << 7) | (0u << 10)                   // A, B = E4M3
          | (static_cast<uint32_t>(n >> 3) << 17)    // N >> 3
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M >> 4
+}
+
+// Instruction descriptor for kind::mxf8f6f4 with block scales: E4M3 x E4M3 ->
+// F32 (implied), both K-major, UE8M0 scale format (bit 23), scale-factor byte
+// selectors for A [29,31) and B [4,6) left at 0.
+__host__ __device__ constexpr uint32_t umma_idesc_mxf8_e4m3_ue8m0(int m, int n) {
+  return (0u << 7) | (0u << 10)                    // A, B = E4M3
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N >> 3
+         | (1u << 23)                               // scale format UE8M0
          | (static_cast<uint32_t>(m >> 4) << 24);   // M >> 4
 }
 

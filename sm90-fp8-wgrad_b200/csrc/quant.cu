@@ -85,6 +85,15 @@ __device__ __forceinline__ float div_rn_by_scale(float x, float s, float rs, boo
   return __int_as_float(__float_as_int(q1) | (__float_as_int(x) & static_cast<int>(0x80000000u)));
 }
 
+// Smallest power of two >= s, for a positive normal s (the clamped scale is at
+// least 1e-12): a set mantissa bit moves the value up to the next exponent.
+// Infinity and NaN stay as they are.
+__device__ __forceinline__ float round_up_pow2(float s) {
+  const uint32_t bits = __float_as_uint(s);
+  if ((bits & 0x7F800000u) == 0x7F800000u || (bits & 0x7FFFFFu) == 0u) return s;
+  return __uint_as_float((bits & 0xFF800000u) + 0x800000u);
+}
+
 // grid: (total_blocks, ceil(cols / QTile<T>::COLS)); block: 256 threads.
 // Destination of the quantised bytes: column c's byte k of block b goes to
 // q[c * pitch + row_start[b] + k] (row_start == nullptr: block_rows * b, the
@@ -103,7 +112,7 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
                                                                   const int32_t* __restrict__ block_row_count,
                                                                   QuantDst d0, QuantDst d1,
                                                                   float* __restrict__ scales, bool vec_ok,
-                                                                  int block_rows, int64_t x_rows) {
+                                                                  int block_rows, int64_t x_rows, bool ue8m0) {
   using Q = QTile<T>;
   // The tile keeps the input type (16 KB BF16, 32 KB fp32): row-major 16-byte writes, and the
   // column walks below read 32 consecutive columns per warp, so neither side
@@ -169,7 +178,8 @@ __global__ void __launch_bounds__(QTHREADS) quantize_1x128_kernel(const T* __res
     float amax = s_amax[0][tid];
 #pragma unroll
     for (int pp = 1; pp < Q::PARTS; ++pp) amax = fmaxf(amax, s_amax[pp][tid]);
-    const float scale = fmaxf(__fdiv_rn(amax, 448.0f), 1.0e-12f);
+    float scale = fmaxf(__fdiv_rn(amax, 448.0f), 1.0e-12f);
+    if (ue8m0) scale = round_up_pow2(scale);
     s_scale[tid] = scale;
     if (tid < ncols) scales[static_cast<int64_t>(b) * cols + c0 + tid] = scale;
   }
@@ -239,7 +249,7 @@ cudaError_t launch_quantize_1x128(const void* x, int x_dtype, int64_t cols, cons
                                   const int32_t* block_row_start, const int32_t* block_row_count,
                                   int64_t total_blocks, void* q, int64_t q_pitch, const int32_t* q_row_start,
                                   bool q_zero_fill, void* kq, int64_t kq_pitch, const int32_t* kq_row_start,
-                                  float* scales, int block_rows, int64_t x_rows, cudaStream_t stream) {
+                                  float* scales, int block_rows, int64_t x_rows, bool ue8m0, cudaStream_t stream) {
   if (total_blocks == 0 || cols == 0) return cudaSuccess;
   const int strip = x_dtype == 0 ? QTile<__nv_bfloat16>::COLS : QTile<float>::COLS;
   const dim3 grid(static_cast<unsigned>(total_blocks), static_cast<unsigned>((cols + strip - 1) / strip));
@@ -249,12 +259,12 @@ cudaError_t launch_quantize_1x128(const void* x, int x_dtype, int64_t cols, cons
     const bool vec_ok = (cols % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
     quantize_1x128_kernel<__nv_bfloat16><<<grid, QTHREADS, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(x), cols, gather_idx, block_row_start, block_row_count, d0, d1, scales,
-        vec_ok, block_rows, x_rows);
+        vec_ok, block_rows, x_rows, ue8m0);
   } else {
     const bool vec_ok = (cols % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
     quantize_1x128_kernel<float><<<grid, QTHREADS, 0, stream>>>(static_cast<const float*>(x), cols, gather_idx,
                                                                block_row_start, block_row_count, d0, d1, scales,
-                                                               vec_ok, block_rows, x_rows);
+                                                               vec_ok, block_rows, x_rows, ue8m0);
   }
   return cudaGetLastError();
 }

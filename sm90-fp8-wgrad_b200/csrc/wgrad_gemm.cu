@@ -67,6 +67,11 @@ __device__ unsigned long long g_wgrad_prof[kProfSlots];
 #define WGRAD_PROF_ADD(slot, t0) ((void)0)
 #define WGRAD_PROF_INC(slot) ((void)0)
 #endif
+#if WGRAD_PROFILE
+#define WGRAD_PROF_PTR s_prof
+#else
+#define WGRAD_PROF_PTR nullptr
+#endif
 
 namespace {
 
@@ -152,6 +157,194 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, int tile) 
   return c;
 }
 
+// TMA producer (one thread): for every K block of every tile this CTA owns,
+// the A and B operand tiles into the STAGES-deep ring and the block's A / B
+// scale vectors into the SCALE_STAGES-deep scale ring.
+template <class C, int BN>
+__device__ __forceinline__ void run_producer(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GemmParams& p,
+                                             uint8_t* s_a, uint8_t* s_b, float* s_scale, uint64_t* full_bar,
+                                             uint64_t* empty_bar, uint64_t* sfull_bar, uint64_t* sempty_bar,
+                                             volatile int* abort_flag, unsigned long long* s_prof) {
+#if WGRAD_PROFILE
+  const bool prof_lane = true;  // called by the producer lane only
+#else
+  (void)s_prof;
+#endif
+  int stage = 0, sstage = 0;
+  uint32_t phase = 0, sphase = 0;
+  for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+    const TileCoord tc = decode_tile(p, tile);
+    const int kb0 = __ldg(p.block_offsets + tc.e);
+    const int nkb = __ldg(p.block_offsets + tc.e + 1) - kb0;
+    const int krow0 = __ldg(p.k_row_offsets + tc.e);
+    const uint32_t a_scale_bytes = static_cast<uint32_t>(min(BM, p.m - tc.m0)) * 4u;
+    const uint32_t b_scale_bytes = static_cast<uint32_t>(min(BN, p.n - tc.n0)) * 4u;
+    bool ok = true;
+    for (int kb = 0; kb < nkb && ok; ++kb) {
+      WGRAD_PROF_T(tw0);
+      ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, kDevTimeoutProducer);
+      WGRAD_PROF_ADD(kProfProducerWaitStage, tw0);
+      if (!ok) break;
+      mbar_arrive_expect_tx(&full_bar[stage], C::A_BYTES + C::B_BYTES);
+      // Test-only failure injection: announce the first stage's bytes but
+      // issue no copy, so the stage never fills and the bounded waits of
+      // the consumers expire (device error word, clean exit).
+      if (!(p.inject == kInjectWithholdFirstLoad && tile == static_cast<int>(blockIdx.x) && kb == 0)) {
+        tma_load_2d(s_a + stage * C::A_BYTES, &tmap_a, &full_bar[stage], krow0 + kb * BK, tc.m0);
+        tma_load_2d(s_b + stage * C::B_BYTES, &tmap_b, &full_bar[stage], krow0 + kb * BK, tc.n0);
+      }
+      if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+
+      WGRAD_PROF_T(tw1);
+      ok = mbar_wait(&sempty_bar[sstage], sphase ^ 1u, abort_flag, kDevTimeoutProducer);
+      WGRAD_PROF_ADD(kProfProducerWaitScales, tw1);
+      if (!ok) break;
+      float* dst = s_scale + sstage * C::SCALE_FLOATS;
+      const size_t blk = static_cast<size_t>(kb0 + kb);
+      mbar_arrive_expect_tx(&sfull_bar[sstage], a_scale_bytes + b_scale_bytes);
+      bulk_load_1d(dst, p.sa + blk * p.m + tc.m0, a_scale_bytes, &sfull_bar[sstage]);
+      bulk_load_1d(dst + BM, p.sb + blk * p.n + tc.n0, b_scale_bytes, &sfull_bar[sstage]);
+      if (++sstage == SCALE_STAGES) { sstage = 0; sphase ^= 1u; }
+    }
+    if (!ok) break;
+  }
+}
+
+// Writes one warp's finished 32 rows x COLS columns (fin, fp32) of tile tc:
+// BF16 (or fp32) into the warp's 128B-swizzled staging area, then TMA stores
+// of 32-row boxes clipped to the output; with accumulate the previous output
+// boxes are first loaded through the same tensor map and added. The caller
+// has waited for the warp's previous store to finish reading the staging
+// area. Returns false when a wait gave up.
+template <int COLS, int OUT_STAGE_BYTES>
+__device__ __forceinline__ bool store_warp_tile(float (&fin)[COLS], const CUtensorMap& tmap_out, const GemmParams& p,
+                                                const TileCoord& tc, int quarter, int lane, int col0,
+                                                uint8_t* stage_out, uint64_t* oldout_bar, uint32_t& oldout_phase,
+                                                volatile int* abort_flag) {
+  const uint32_t stage_addr = smem_u32(stage_out);
+  bool ok = true;
+  const bool rows_in = (tc.m0 + quarter * 32) < p.m;
+  const uint32_t swz = static_cast<uint32_t>(lane & 7);
+  // accumulate: the previous output boxes come in through the same tensor
+  // map and 128B-swizzled staging layout the store uses (TMA load into this
+  // warp's staging area, bounded wait), so each thread adds its own row.
+  auto load_previous = [&](int nboxes, int box_cols, int first_box) -> bool {
+    if (lane == 0) {
+      uint32_t bytes = 0;
+      for (int b = 0; b < nboxes; ++b) bytes += col0 + (first_box + b) * box_cols < p.n ? 4096u : 0u;
+      mbar_arrive_expect_tx(oldout_bar, bytes);
+      for (int b = 0; b < nboxes; ++b) {
+        const int c = col0 + (first_box + b) * box_cols;
+        if (c < p.n) tma_load_3d(stage_out + b * 4096, &tmap_out, oldout_bar, c, tc.m0 + quarter * 32, tc.e);
+      }
+    }
+    const bool landed = mbar_wait(oldout_bar, oldout_phase, abort_flag, kDevTimeoutEpilogue);
+    if (!landed) {
+      // Giving up (timeout, or another role aborted): let this warp's own
+      // load land before the CTA exits. Bounded, regardless of the abort flag.
+      const uint32_t addr = smem_u32(oldout_bar);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(addr, oldout_phase) && globaltimer_ns() - t0 < WGRAD_WAIT_TIMEOUT_NS) {
+      }
+    }
+    oldout_phase ^= 1u;
+    return __all_sync(0xffffffffu, landed);
+  };
+  if (!p.out_f32) {
+    // bf16: boxes of 32 rows x 64 columns (128 B rows, 128B swizzle), 4 KB each.
+    constexpr int BOXES = COLS / 64;
+    if (p.accumulate && rows_in) {
+      ok = load_previous(BOXES, 64, 0);
+      if (!ok) return false;
+#pragma unroll
+      for (int bx = 0; bx < BOXES; ++bx) {
+        const uint32_t box = stage_addr + bx * 4096 + lane * 128;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const uint4 w = ld_shared_v4(box + ((ch ^ swz) << 4));
+          const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+          float* v = &fin[bx * 64 + ch * 8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ww[i]));
+            v[2 * i] += f.x;
+            v[2 * i + 1] += f.y;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int bx = 0; bx < BOXES; ++bx) {
+      const uint32_t box = stage_addr + bx * 4096 + lane * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const float* v = &fin[bx * 64 + ch * 8];
+        st_shared_v4(box + ((ch ^ swz) << 4), pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                     pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && rows_in) {
+#pragma unroll
+      for (int bx = 0; bx < BOXES; ++bx) {
+        const int c = col0 + bx * 64;
+        if (c < p.n) tma_store_3d(&tmap_out, stage_out + bx * 4096, c, tc.m0 + quarter * 32, tc.e);
+      }
+      bulk_commit_group();
+    }
+  } else {
+    // fp32: boxes of 32 rows x 32 columns, PER_ROUND boxes per staging round.
+    constexpr int BOXES = COLS / 32;
+    constexpr int PER_ROUND = OUT_STAGE_BYTES / 4096;
+#pragma unroll
+    for (int bx0 = 0; bx0 < BOXES; bx0 += PER_ROUND) {
+      if (bx0 > 0) {
+        if (lane == 0) bulk_wait_group_read0();
+        __syncwarp();
+      }
+      if (p.accumulate && rows_in) {
+        ok = load_previous(PER_ROUND, 32, bx0);
+        if (!ok) return false;
+#pragma unroll
+        for (int bi = 0; bi < PER_ROUND; ++bi) {
+          const uint32_t box = stage_addr + bi * 4096 + lane * 128;
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            const uint4 w = ld_shared_v4(box + ((ch ^ swz) << 4));
+            float* v = &fin[(bx0 + bi) * 32 + ch * 4];
+            v[0] += __uint_as_float(w.x);
+            v[1] += __uint_as_float(w.y);
+            v[2] += __uint_as_float(w.z);
+            v[3] += __uint_as_float(w.w);
+          }
+        }
+      }
+#pragma unroll
+      for (int bi = 0; bi < PER_ROUND; ++bi) {
+        const uint32_t box = stage_addr + bi * 4096 + lane * 128;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const float* v = &fin[(bx0 + bi) * 32 + ch * 4];
+          st_shared_v4(box + ((ch ^ swz) << 4), __float_as_uint(v[0]), __float_as_uint(v[1]),
+                       __float_as_uint(v[2]), __float_as_uint(v[3]));
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && rows_in) {
+#pragma unroll
+        for (int bi = 0; bi < PER_ROUND; ++bi) {
+          const int c = col0 + (bx0 + bi) * 32;
+          if (c < p.n) tma_store_3d(&tmap_out, stage_out + bi * 4096, c, tc.m0 + quarter * 32, tc.e);
+        }
+        bulk_commit_group();
+      }
+    }
+  }
+  return ok;
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_SM)
     grouped_wgrad_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -217,46 +410,8 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int stage = 0, sstage = 0;
-      uint32_t phase = 0, sphase = 0;
-      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-        const TileCoord tc = decode_tile(p, tile);
-        const int kb0 = __ldg(p.block_offsets + tc.e);
-        const int nkb = __ldg(p.block_offsets + tc.e + 1) - kb0;
-        const int krow0 = __ldg(p.k_row_offsets + tc.e);
-        const uint32_t a_scale_bytes = static_cast<uint32_t>(min(BM, p.m - tc.m0)) * 4u;
-        const uint32_t b_scale_bytes = static_cast<uint32_t>(min(BN, p.n - tc.n0)) * 4u;
-        bool ok = true;
-        for (int kb = 0; kb < nkb && ok; ++kb) {
-          WGRAD_PROF_T(tw0);
-          ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, kDevTimeoutProducer);
-          WGRAD_PROF_ADD(kProfProducerWaitStage, tw0);
-          if (!ok) break;
-          mbar_arrive_expect_tx(&full_bar[stage], C::A_BYTES + C::B_BYTES);
-          // Test-only failure injection: announce the first stage's bytes but
-          // issue no copy, so the stage never fills and the bounded waits of
-          // the consumers expire (device error word, clean exit).
-          if (!(p.inject == kInjectWithholdFirstLoad && tile == static_cast<int>(blockIdx.x) && kb == 0)) {
-            tma_load_2d(s_a + stage * C::A_BYTES, &tmap_a, &full_bar[stage], krow0 + kb * BK, tc.m0);
-            tma_load_2d(s_b + stage * C::B_BYTES, &tmap_b, &full_bar[stage], krow0 + kb * BK, tc.n0);
-          }
-          if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
-
-          WGRAD_PROF_T(tw1);
-          ok = mbar_wait(&sempty_bar[sstage], sphase ^ 1u, abort_flag, kDevTimeoutProducer);
-          WGRAD_PROF_ADD(kProfProducerWaitScales, tw1);
-          if (!ok) break;
-          float* dst = s_scale + sstage * C::SCALE_FLOATS;
-          const size_t blk = static_cast<size_t>(kb0 + kb);
-          mbar_arrive_expect_tx(&sfull_bar[sstage], a_scale_bytes + b_scale_bytes);
-          bulk_load_1d(dst, p.sa + blk * p.m + tc.m0, a_scale_bytes, &sfull_bar[sstage]);
-          bulk_load_1d(dst + BM, p.sb + blk * p.n + tc.n0, b_scale_bytes, &sfull_bar[sstage]);
-          if (++sstage == SCALE_STAGES) { sstage = 0; sphase ^= 1u; }
-        }
-        if (!ok) break;
-      }
-    }
+    if (lane == 0) run_producer<C, BN>(tmap_a, tmap_b, p, s_a, s_b, s_scale, full_bar, empty_bar, sfull_bar, sempty_bar,
+                                       abort_flag, WGRAD_PROF_PTR);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc = umma_idesc_e4m3_f32(BM, BN);
@@ -311,7 +466,6 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
     const int row = quarter * 32 + lane;     // row within the tile == TMEM lane
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     uint8_t* stage_out = s_out + ew * C::OUT_STAGE_BYTES_PER_WARP;
-    const uint32_t stage_out_addr = smem_u32(stage_out);
 
     int acc = 0, sstage = 0;
     uint32_t aphase = 0, sphase = 0, oldout_phase = 0;
@@ -390,9 +544,9 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
       // -------------------------------------------------------- epilogue store
       WGRAD_PROF_T(ts0);
       WGRAD_PROF_INC(kProfTiles);
-      const int g_row = tc.m0 + row;
       const int col0 = tc.n0 + half * C::COLS_PER_WARP;
 #if WGRAD_DEBUG_MODES
+      const int g_row = tc.m0 + row;
       if (p.mode == kModeCoordM || p.mode == kModeCoordN || p.mode == kModeScaleOnly) {
 #pragma unroll
         for (int j = 0; j < C::COLS_PER_WARP; ++j) {
@@ -407,125 +561,8 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
       if (lane == 0) bulk_wait_group_read0();
       __syncwarp();
       WGRAD_PROF_ADD(kProfEpiStoreWait, ts1);
-      const bool rows_in = (tc.m0 + quarter * 32) < p.m;
-      const uint32_t swz = static_cast<uint32_t>(lane & 7);
-      // accumulate: the previous output boxes come in through the same tensor
-      // map and 128B-swizzled staging layout the store uses (TMA load into this
-      // warp's staging area, bounded wait), so each thread adds its own row.
-      auto load_previous = [&](int nboxes, int box_cols, int first_box) -> bool {
-        if (lane == 0) {
-          uint32_t bytes = 0;
-          for (int b = 0; b < nboxes; ++b) bytes += col0 + (first_box + b) * box_cols < p.n ? 4096u : 0u;
-          mbar_arrive_expect_tx(&oldout_bar[ew], bytes);
-          for (int b = 0; b < nboxes; ++b) {
-            const int c = col0 + (first_box + b) * box_cols;
-            if (c < p.n) tma_load_3d(stage_out + b * 4096, &tmap_out, &oldout_bar[ew], c, tc.m0 + quarter * 32, tc.e);
-          }
-        }
-        const bool landed = mbar_wait(&oldout_bar[ew], oldout_phase, abort_flag, kDevTimeoutEpilogue);
-        if (!landed) {
-          // Giving up (timeout, or another role aborted): let this warp's own
-          // load land before the CTA exits. Bounded, regardless of the abort flag.
-          const uint32_t addr = smem_u32(&oldout_bar[ew]);
-          const uint64_t t0 = globaltimer_ns();
-          while (!mbar_try_wait(addr, oldout_phase) && globaltimer_ns() - t0 < WGRAD_WAIT_TIMEOUT_NS) {
-          }
-        }
-        oldout_phase ^= 1u;
-        return __all_sync(0xffffffffu, landed);
-      };
-      if (!p.out_f32) {
-        // bf16: boxes of 32 rows x 64 columns (128 B rows, 128B swizzle), 4 KB each.
-        constexpr int BOXES = C::COLS_PER_WARP / 64;
-        if (p.accumulate && rows_in) {
-          ok = load_previous(BOXES, 64, 0);
-          if (!ok) break;
-#pragma unroll
-          for (int bx = 0; bx < BOXES; ++bx) {
-            const uint32_t box = stage_out_addr + bx * 4096 + lane * 128;
-#pragma unroll
-            for (int ch = 0; ch < 8; ++ch) {
-              const uint4 w = ld_shared_v4(box + ((ch ^ swz) << 4));
-              const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-              float* v = &fin[bx * 64 + ch * 8];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ww[i]));
-                v[2 * i] += f.x;
-                v[2 * i + 1] += f.y;
-              }
-            }
-          }
-        }
-#pragma unroll
-        for (int bx = 0; bx < BOXES; ++bx) {
-          const uint32_t box = stage_out_addr + bx * 4096 + lane * 128;
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            const float* v = &fin[bx * 64 + ch * 8];
-            st_shared_v4(box + ((ch ^ swz) << 4), pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
-                         pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
-          }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && rows_in) {
-#pragma unroll
-          for (int bx = 0; bx < BOXES; ++bx) {
-            const int c = col0 + bx * 64;
-            if (c < p.n) tma_store_3d(&tmap_out, stage_out + bx * 4096, c, tc.m0 + quarter * 32, tc.e);
-          }
-          bulk_commit_group();
-        }
-      } else {
-        // fp32: boxes of 32 rows x 32 columns, PER_ROUND boxes per staging round.
-        constexpr int BOXES = C::COLS_PER_WARP / 32;
-        constexpr int PER_ROUND = C::OUT_STAGE_BYTES_PER_WARP / 4096;
-#pragma unroll
-        for (int bx0 = 0; bx0 < BOXES; bx0 += PER_ROUND) {
-          if (bx0 > 0) {
-            if (lane == 0) bulk_wait_group_read0();
-            __syncwarp();
-          }
-          if (p.accumulate && rows_in) {
-            ok = load_previous(PER_ROUND, 32, bx0);
-            if (!ok) break;
-#pragma unroll
-            for (int bi = 0; bi < PER_ROUND; ++bi) {
-              const uint32_t box = stage_out_addr + bi * 4096 + lane * 128;
-#pragma unroll
-              for (int ch = 0; ch < 8; ++ch) {
-                const uint4 w = ld_shared_v4(box + ((ch ^ swz) << 4));
-                float* v = &fin[(bx0 + bi) * 32 + ch * 4];
-                v[0] += __uint_as_float(w.x);
-                v[1] += __uint_as_float(w.y);
-                v[2] += __uint_as_float(w.z);
-                v[3] += __uint_as_float(w.w);
-              }
-            }
-          }
-#pragma unroll
-          for (int bi = 0; bi < PER_ROUND; ++bi) {
-            const uint32_t box = stage_out_addr + bi * 4096 + lane * 128;
-#pragma unroll
-            for (int ch = 0; ch < 8; ++ch) {
-              const float* v = &fin[(bx0 + bi) * 32 + ch * 4];
-              st_shared_v4(box + ((ch ^ swz) << 4), __float_as_uint(v[0]), __float_as_uint(v[1]),
-                           __float_as_uint(v[2]), __float_as_uint(v[3]));
-            }
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && rows_in) {
-#pragma unroll
-            for (int bi = 0; bi < PER_ROUND; ++bi) {
-              const int c = col0 + (bx0 + bi) * 32;
-              if (c < p.n) tma_store_3d(&tmap_out, stage_out + bi * 4096, c, tc.m0 + quarter * 32, tc.e);
-            }
-            bulk_commit_group();
-          }
-        }
-      }
+      ok = store_warp_tile<C::COLS_PER_WARP, C::OUT_STAGE_BYTES_PER_WARP>(
+          fin, tmap_out, p, tc, quarter, lane, col0, stage_out, &oldout_bar[ew], oldout_phase, abort_flag);
       if (!ok) break;
       WGRAD_PROF_ADD(kProfEpiStore, ts0);
     }
@@ -538,6 +575,277 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
 #if WGRAD_PROFILE
   if (threadIdx.x < kProfSlots) atomicAdd(&g_wgrad_prof[threadIdx.x], s_prof[threadIdx.x]);
 #endif
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// UE8M0 variant: scales that are powers of two are applied by the tensor core
+// (tcgen05.mma kind::mxf8f6f4.block_scale, one E8M0 scale per row of A / B
+// and 32-wide K slice), so a tile's K blocks accumulate in one TMEM buffer and
+// no fp32 promotion runs. Exact for such scales: the sum is the same
+// sum_b sum_k qa qb sa sb, rounded once per UMMA instead of once per K block.
+//
+// Warps: 0 TMA producer (shared with the promotion kernel), 1 MMA issuer,
+// 4..7 scale-factor writers, 8..19 epilogue (three 64-column warps per TMEM
+// lane quarter). TMEM: two 192-column accumulators, then SF_STAGES
+// scale-factor stages of 16 columns (A: 4 columns, B: 8 columns from +4).
+// Scale-factor layout in TMEM (one 32-bit word per lane and column, the
+// layout tcgen05.cp 32x128b.warpx4 writes from the CUTLASS Sm1xx block-scaled
+// atom): row r of A or B sits in lane r % 32, column r / 32, and byte j of the
+// word is the scale of K slice j; every lane quarter holds the same copy.
+// Each writer warp fills its own lane quarter with tcgen05.st. The four K
+// slices of a 128-row block share one scale, so all four bytes are equal and
+// the byte selectors of the instruction descriptor stay 0.
+struct BsCfg {
+  static constexpr int BN = 192;
+  static constexpr int STAGES = 4;
+  static constexpr int FIRST_SF_WARP = 4;
+  static constexpr int SF_WARPS = 4;
+  static constexpr int FIRST_EPI = 8;
+  static constexpr int EPI_WARPS = 12;
+  static constexpr int THREADS = 32 * (FIRST_EPI + EPI_WARPS);
+  static constexpr int COLS_PER_WARP = BN / (EPI_WARPS / 4);  // 64
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int SCALE_FLOATS = BM + BN;
+  static constexpr int OUT_STAGE_BYTES_PER_WARP = 4096;
+  static constexpr int SF_STAGES = 4;
+  static constexpr int SF_COL0 = 2 * BN;
+  static constexpr int SF_STAGE_COLS = 16;
+  static constexpr int SF_B_OFFSET = 4;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + EPI_WARPS * OUT_STAGE_BYTES_PER_WARP +
+                                    SCALE_STAGES * SCALE_FLOATS * 4 + 512 /*barriers*/ + 1024 /*align*/;
+  static_assert(SF_COL0 + SF_STAGES * SF_STAGE_COLS <= TMEM_COLS, "TMEM columns");
+  static_assert(COLS_PER_WARP * 32 * 2 == OUT_STAGE_BYTES_PER_WARP, "one BF16 staging round per tile");
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
+};
+
+// E8M0 byte of a positive power-of-two fp32 scale, replicated into the four
+// bytes of a TMEM word. Anything else (mantissa bits, zero, subnormal, inf,
+// NaN, negative) sets device error 6 and encodes as 1.0.
+__device__ __forceinline__ uint32_t e8m0_word(float s) {
+  const uint32_t bits = __float_as_uint(s);
+  const uint32_t e = bits >> 23;  // sign bit set -> e > 255
+  if ((bits & 0x7FFFFFu) != 0u || e == 0u || e >= 255u) {
+    record_device_error(kDevScaleNotPow2);
+    return 127u * 0x01010101u;
+  }
+  return e * 0x01010101u;
+}
+
+__global__ void __launch_bounds__(BsCfg::THREADS, 1)
+    grouped_wgrad_ue8m0_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                               const __grid_constant__ CUtensorMap tmap_out, const GemmParams p) {
+  using C = BsCfg;
+  constexpr int BN = C::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_a = smem;
+  uint8_t* s_b = s_a + C::STAGES * C::A_BYTES;
+  uint8_t* s_out = s_b + C::STAGES * C::B_BYTES;
+  float* s_scale = reinterpret_cast<float*>(s_out + C::EPI_WARPS * C::OUT_STAGE_BYTES_PER_WARP);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_scale + SCALE_STAGES * C::SCALE_FLOATS);
+  uint64_t* full_bar = bars;                             // [STAGES]      TMA -> MMA
+  uint64_t* empty_bar = full_bar + C::STAGES;            // [STAGES]      MMA -> TMA
+  uint64_t* sfull_bar = empty_bar + C::STAGES;           // [SCALE_STAGES] TMA -> SF writers
+  uint64_t* sempty_bar = sfull_bar + SCALE_STAGES;       // [SCALE_STAGES] SF writers -> TMA
+  uint64_t* sffull_bar = sempty_bar + SCALE_STAGES;      // [SF_STAGES]   SF writers -> MMA
+  uint64_t* sfempty_bar = sffull_bar + C::SF_STAGES;     // [SF_STAGES]   MMA -> SF writers
+  uint64_t* tfull_bar = sfempty_bar + C::SF_STAGES;      // [2] MMA -> epilogue
+  uint64_t* tempty_bar = tfull_bar + 2;                  // [2] epilogue -> MMA
+  uint64_t* oldout_bar = tempty_bar + 2;                 // [EPI_WARPS] previous output (accumulate)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(oldout_bar + C::EPI_WARPS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::STAGES; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < SCALE_STAGES; ++i) {
+      mbar_init(&sfull_bar[i], 1);
+      mbar_init(&sempty_bar[i], C::SF_WARPS);
+    }
+    for (int i = 0; i < C::SF_STAGES; ++i) {
+      mbar_init(&sffull_bar[i], C::SF_WARPS);
+      mbar_init(&sfempty_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], C::EPI_WARPS);
+    }
+    for (int i = 0; i < C::EPI_WARPS; ++i) mbar_init(&oldout_bar[i], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0 && p.has_operands) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+    tma_prefetch_desc(&tmap_out);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) run_producer<C, BN>(tmap_a, tmap_b, p, s_a, s_b, s_scale, full_bar, empty_bar, sfull_bar, sempty_bar,
+                                       abort_flag, nullptr);
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = umma_idesc_mxf8_e4m3_ue8m0(BM, BN);
+    int stage = 0, sfs = 0, acc = 0;
+    uint32_t phase = 0, sfphase = 0, aphase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      const TileCoord tc = decode_tile(p, tile);
+      const int nkb = __ldg(p.block_offsets + tc.e + 1) - __ldg(p.block_offsets + tc.e);
+      if (nkb == 0) continue;  // empty expert: the epilogue writes zeros without the accumulator
+      const int klen = __ldg(p.k_row_offsets + tc.e + 1) - __ldg(p.k_row_offsets + tc.e);
+      const int last_atoms = min(4, max(1, (klen - (nkb - 1) * BK + 31) / 32));
+      ok = mbar_wait(&tempty_bar[acc], aphase ^ 1u, abort_flag, kDevTimeoutMma);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int atoms = kb + 1 == nkb ? last_atoms : BK / 32;
+        ok = mbar_wait2(&full_bar[stage], phase, &sffull_bar[sfs], sfphase, abort_flag, kDevTimeoutMma);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_addr = smem_u32(s_a + stage * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(s_b + stage * C::B_BYTES);
+          const uint32_t sfa = tmem_base + static_cast<uint32_t>(C::SF_COL0 + sfs * C::SF_STAGE_COLS);
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            if (k >= atoms) break;
+            umma_mxf8(d_tmem, umma_desc_k_sw128(a_addr + k * 32), umma_desc_k_sw128(b_addr + k * 32), idesc, sfa,
+                      sfa + C::SF_B_OFFSET, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          umma_commit(&sfempty_bar[sfs]);
+        }
+        __syncwarp();
+        if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+        if (++sfs == C::SF_STAGES) { sfs = 0; sfphase ^= 1u; }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&tfull_bar[acc]);
+      __syncwarp();
+      acc ^= 1;
+      if (acc == 0) aphase ^= 1u;
+    }
+  } else if (warp >= C::FIRST_SF_WARP && warp < C::FIRST_EPI) {
+    // ------------------------------------------------------------ scale-factor writers
+    const int quarter = warp & 3;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    int sstage = 0, sfs = 0;
+    uint32_t sphase = 0, sfphase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      const TileCoord tc = decode_tile(p, tile);
+      const int nkb = __ldg(p.block_offsets + tc.e + 1) - __ldg(p.block_offsets + tc.e);
+      const int a_valid = min(BM, p.m - tc.m0);
+      const int b_valid = min(BN, p.n - tc.n0);
+      for (int kb = 0; kb < nkb; ++kb) {
+        ok = mbar_wait2(&sfull_bar[sstage], sphase, &sfempty_bar[sfs], sfphase ^ 1u, abort_flag, kDevTimeoutEpilogue);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const float* sc = s_scale + sstage * C::SCALE_FLOATS;
+        uint32_t wa[4], wb[8];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int r = lane + 32 * c;
+          wa[c] = r < a_valid ? e8m0_word(sc[r]) : 127u * 0x01010101u;
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int r = lane + 32 * c;
+          wb[c] = (r < BN && r < b_valid) ? e8m0_word(sc[BM + r]) : 127u * 0x01010101u;
+        }
+        const uint32_t t = tmem_base + lane_addr + static_cast<uint32_t>(C::SF_COL0 + sfs * C::SF_STAGE_COLS);
+        tmem_st_32x32b_x4(t, wa[0], wa[1], wa[2], wa[3]);
+        tmem_st_32x32b_x8(t + C::SF_B_OFFSET, wb);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&sempty_bar[sstage]);
+          mbar_arrive(&sffull_bar[sfs]);
+        }
+        if (++sstage == SCALE_STAGES) { sstage = 0; sphase ^= 1u; }
+        if (++sfs == C::SF_STAGES) { sfs = 0; sfphase ^= 1u; }
+      }
+    }
+  } else if (warp >= C::FIRST_EPI) {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - C::FIRST_EPI;   // 0 .. EPI_WARPS-1
+    const int quarter = warp & 3;
+    const int cgroup = ew >> 2;           // 64-column group of the tile
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    uint8_t* stage_out = s_out + ew * C::OUT_STAGE_BYTES_PER_WARP;
+    int acc = 0;
+    uint32_t aphase = 0, oldout_phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      const TileCoord tc = decode_tile(p, tile);
+      const int nkb = __ldg(p.block_offsets + tc.e + 1) - __ldg(p.block_offsets + tc.e);
+      float fin[C::COLS_PER_WARP];
+      if (nkb == 0) {
+#pragma unroll
+        for (int j = 0; j < C::COLS_PER_WARP; ++j) fin[j] = 0.f;
+      } else {
+        ok = mbar_wait(&tfull_bar[acc], aphase, abort_flag, kDevTimeoutEpilogue);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t t_addr =
+            tmem_base + lane_addr + static_cast<uint32_t>(acc * BN + cgroup * C::COLS_PER_WARP);
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(t_addr, r0);
+        tmem_ld_32x32b_x32(t_addr + 32, r1);
+        tmem_wait_ld_bind(r0);
+        tmem_wait_ld_bind(r1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          fin[j] = __uint_as_float(r0[j]);
+          fin[32 + j] = __uint_as_float(r1[j]);
+        }
+        acc ^= 1;
+        if (acc == 0) aphase ^= 1u;
+      }
+      const int col0 = tc.n0 + cgroup * C::COLS_PER_WARP;
+      // The previous tile's TMA store must have finished reading the staging buffer.
+      if (lane == 0) bulk_wait_group_read0();
+      __syncwarp();
+      ok = store_warp_tile<C::COLS_PER_WARP, C::OUT_STAGE_BYTES_PER_WARP>(
+          fin, tmap_out, p, tc, quarter, lane, col0, stage_out, &oldout_bar[ew], oldout_phase, abort_flag);
+    }
+    if (lane == 0) bulk_wait_group0();  // all output writes complete before exit
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
@@ -564,8 +872,25 @@ static cudaError_t launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, con
   return cudaGetLastError();
 }
 
+static cudaError_t launch_ue8m0(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                                const GemmParams& p, int grid, cudaStream_t stream) {
+  static int configured_device_mask = 0;  // bit per device ordinal (< 32)
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev >= 32 || !(configured_device_mask & (1 << dev))) {
+    err = cudaFuncSetAttribute(grouped_wgrad_ue8m0_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               BsCfg::SMEM_BYTES);
+    if (err != cudaSuccess) return err;
+    if (dev < 32) configured_device_mask |= (1 << dev);
+  }
+  grouped_wgrad_ue8m0_kernel<<<grid, BsCfg::THREADS, BsCfg::SMEM_BYTES, stream>>>(ta, tb, to, p);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_grouped_wgrad(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                                  const GemmParams& p, int grid, cudaStream_t stream) {
+  if (p.ue8m0) return p.bn == BsCfg::BN ? launch_ue8m0(ta, tb, to, p, grid, stream) : cudaErrorInvalidValue;
   if (p.bn == 256) {
     return p.epi_warps == 16 ? launch_impl<256, 16>(ta, tb, to, p, grid, stream)
                              : launch_impl<256, 8>(ta, tb, to, p, grid, stream);

@@ -62,6 +62,7 @@ struct GemmParams {
   int epi_warps;                // promotion warps: 8, or 16 (bn 256 only)
   int inject;                   // test-only failure injection (kInject*), 0 in normal use
   int mode;                     // KernelMode; only instrumented builds honour a non-zero mode
+  int ue8m0;                    // 1: scales are powers of two, applied by block-scaled UMMAs (bn 192)
 };
 
 cudaError_t launch_grouped_wgrad(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,

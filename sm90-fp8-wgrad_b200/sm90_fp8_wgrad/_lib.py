@@ -34,6 +34,9 @@ TILE_128x256_W8 = 3
 TILE_128x256_W16 = 4
 TILE_128x128_2CTA = 5
 TILE_128x192_W12 = 6
+TILE_128x192_UE8M0 = 7
+SCALE_FP32 = 0
+SCALE_UE8M0 = 1
 
 # Every symbol include/sm100_fp8_wgrad.h declares.
 EXPORTED_SYMBOLS = (
@@ -91,6 +94,7 @@ class Sm100WgradQuantArgs(ctypes.Structure):
         ("scales", ctypes.c_void_p),
         ("block_rows", ctypes.c_int32),
         ("x_rows", ctypes.c_int64),
+        ("scale_format", ctypes.c_int32),
     ]
 
 

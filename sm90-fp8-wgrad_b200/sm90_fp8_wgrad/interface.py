@@ -63,6 +63,7 @@ TUNED_CONFIGS: dict[str, int] = {
     "sm100_128x256_w16": _lib.TILE_128x256_W16,   # 16 promotion warps
     "sm100_128x128_2cta": _lib.TILE_128x128_2CTA,  # two 128x128 pipelines (CTAs) per SM
     "sm100_128x192_w12": _lib.TILE_128x192_W12,    # 192-column tile, 12 promotion warps
+    "sm100_128x192_ue8m0": _lib.TILE_128x192_UE8M0,  # power-of-two scales as tensor-core block scales
 }
 
 
@@ -158,6 +159,11 @@ def fp8_grouped_wgrad_sm90(
     expert range of the same operands and metadata, bit-identical to the
     corresponding slice of a full launch. It lets a caller overlap the
     device-to-host copy of finished experts with the rest of the GEMM.
+
+    When both operands carry ``scale_format == "ue8m0"`` (power-of-two
+    scales from ``quantize_grouped_wgrad_operand_128x1(..., scale_format="ue8m0")``),
+    the default config runs the block-scaled kernel: the same sum, with the
+    scales applied inside the tensor core instead of a per-block fp32 promotion.
     """
     kernel_mode = _kernel_mode()
     layout_mode = resolve_wgrad_layout_mode()
@@ -270,6 +276,12 @@ def fp8_grouped_wgrad_sm90(
         args.block_offsets = meta.block_offsets.data_ptr() + 4 * e0
         args.k_row_offsets = k_row_offsets.data_ptr() + 4 * e0
         args.expert_order = None
+    ue8m0_operands = all(getattr(op, "scale_format", "fp32") == "ue8m0" for op in (lhs, rhs))
+    if resolved == "sm100_128x192_ue8m0" and not ue8m0_operands:
+        raise RuntimeError("tuned_config 'sm100_128x192_ue8m0' needs both operands quantised with scale_format='ue8m0'")
+    if TUNED_CONFIGS[resolved] == _lib.TILE_AUTO and ue8m0_operands and kernel_mode == "normal":
+        # Power-of-two scales on both sides: the tensor core applies them, no fp32 promotion.
+        resolved = "sm100_128x192_ue8m0"
     args.tile_config = TUNED_CONFIGS[resolved]
     args.max_ctas = int(os.environ.get("SM100_WGRAD_MAX_CTAS", "0") or 0)
     lib = _lib.load()

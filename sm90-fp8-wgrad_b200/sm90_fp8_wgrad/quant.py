@@ -40,11 +40,24 @@ FP8_SCALE_EPS = 1.0e-12
 class Fp8GroupedWgradOperand:
     """FP8 operand: ``data`` logical [K_rows, cols] (stride (1, pitch)),
     ``scales`` [total_blocks, cols] fp32; ``kernel_data`` is the packed-layout
-    launch copy [cols, K] (unused by the padded layout)."""
+    launch copy [cols, K] (unused by the padded layout). ``scale_format``
+    "ue8m0" marks scales that the quantiser rounded up to powers of two; the
+    GEMM then applies them as tensor-core block scales (still stored as fp32).
+    """
 
     data: torch.Tensor
     scales: torch.Tensor
     kernel_data: torch.Tensor | None = None
+    scale_format: str = "fp32"
+
+
+SCALE_FORMATS = ("fp32", "ue8m0")
+
+
+def _check_scale_format(scale_format: str) -> int:
+    if scale_format not in SCALE_FORMATS:
+        raise RuntimeError(f"scale_format must be one of {SCALE_FORMATS}, got {scale_format!r}")
+    return _lib.SCALE_UE8M0 if scale_format == "ue8m0" else _lib.SCALE_FP32
 
 
 # ------------------------------------------------------- packed-layout helpers
@@ -91,8 +104,9 @@ def operand_pitch(k_rows: int) -> int:
 
 
 def _quantize(x: torch.Tensor, gather_idx: torch.Tensor | None, meta: WgradScaleBlockMeta,
-              layout_mode: str | None) -> Fp8GroupedWgradOperand:
+              layout_mode: str | None, scale_format: str = "fp32") -> Fp8GroupedWgradOperand:
     """Shared body of the two quantiser entry points (one CUDA launch)."""
+    fmt = _check_scale_format(scale_format)
     if x.ndim != 2:
         raise RuntimeError(f"expected x_grouped [valid_TK,N], got {tuple(x.shape)}")
     if not x.is_cuda:
@@ -125,6 +139,7 @@ def _quantize(x: torch.Tensor, gather_idx: torch.Tensor | None, meta: WgradScale
     args.scales = scales.data_ptr()
     args.block_rows = block_rows
     args.x_rows = int(x.shape[0])
+    args.scale_format = fmt
     kernel_q = None
     if mode == LAYOUT_MODE_PADDED:
         q_rows = int(meta.padded_rows)
@@ -156,7 +171,7 @@ def _quantize(x: torch.Tensor, gather_idx: torch.Tensor | None, meta: WgradScale
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream().cuda_stream
         _lib.check(lib.sm100_wgrad_quantize_1x128_ex(ctypes.byref(args), stream), "sm100_wgrad_quantize_1x128_ex")
-    return Fp8GroupedWgradOperand(q, scales, kernel_data=kernel_q)
+    return Fp8GroupedWgradOperand(q, scales, kernel_data=kernel_q, scale_format=scale_format)
 
 
 def quantize_grouped_wgrad_operand_128x1(
@@ -165,9 +180,15 @@ def quantize_grouped_wgrad_operand_128x1(
     *,
     block_n: int = 32,
     layout_mode: str | None = None,
+    scale_format: str = "fp32",
 ) -> Fp8GroupedWgradOperand:
     """Quantise expert-major grouped rows [valid_rows, cols] (BF16 or fp32)
     into an FP8 operand with 1x128 fp32 scales (reference quant.py:175-270).
+
+    ``scale_format`` "fp32" (default) is the reference's scale
+    max(amax / 448, 1e-12); "ue8m0" rounds that scale up to the next power of
+    two (an extension: the reference has no such mode), so that
+    ``fp8_grouped_wgrad_sm90`` can apply it as a tensor-core block scale.
 
     ``layout_mode`` "padded" stores each expert in whole 128-row slots
     (zero-filled tails); "packed" stores ``data`` on the valid rows only and a
@@ -177,7 +198,7 @@ def quantize_grouped_wgrad_operand_128x1(
     (the CUDA kernel tiles 64 columns per CTA).
     """
     del block_n
-    return _quantize(x_grouped, None, meta, layout_mode)
+    return _quantize(x_grouped, None, meta, layout_mode, scale_format)
 
 
 def quantize_grouped_wgrad_operand_128x1_gather(
@@ -186,6 +207,7 @@ def quantize_grouped_wgrad_operand_128x1_gather(
     meta: WgradScaleBlockMeta,
     *,
     layout_mode: str | None = None,
+    scale_format: str = "fp32",
 ) -> Fp8GroupedWgradOperand:
     """Gather + quantise in one pass: row r of the expert-major operand is row
     ``gather_idx[r]`` of the token-major activation ``x`` [tokens, cols].
@@ -201,7 +223,7 @@ def quantize_grouped_wgrad_operand_128x1_gather(
     if gather_idx.device != x.device:
         raise RuntimeError("gather_idx and x must be on the same device")
     idx = gather_idx if gather_idx.dtype == torch.int32 else gather_idx.to(torch.int32)
-    return _quantize(x, idx.contiguous(), meta, layout_mode)
+    return _quantize(x, idx.contiguous(), meta, layout_mode, scale_format)
 
 
 def quantize_grouped_wgrad_operand_tail_k(

@@ -156,6 +156,7 @@ def make_synthetic_wgrad_inputs(
     grad_std: float = 0.01,
     expert_range: tuple[int, int] | None = None,
     routing: Routing | None = None,
+    scale_format: str = "fp32",
 ) -> SyntheticWgradInputs:
     if device is None:
         if not torch.cuda.is_available():
@@ -194,10 +195,14 @@ def make_synthetic_wgrad_inputs(
     x_grouped = x.index_select(0, gather).contiguous()
 
     if build_fp8_operands:
-        grad_y_q = quantize_grouped_wgrad_operand_128x1(grad_y_grouped, meta, layout_mode=layout_mode)
-        hidden_q = quantize_grouped_wgrad_operand_128x1(hidden_grouped, meta, layout_mode=layout_mode)
-        grad_gate_up_q = quantize_grouped_wgrad_operand_128x1(grad_gate_up_grouped, meta, layout_mode=layout_mode)
-        x_q = quantize_grouped_wgrad_operand_128x1(x_grouped, meta, layout_mode=layout_mode)
+        grad_y_q = quantize_grouped_wgrad_operand_128x1(grad_y_grouped, meta, layout_mode=layout_mode,
+                                                        scale_format=scale_format)
+        hidden_q = quantize_grouped_wgrad_operand_128x1(hidden_grouped, meta, layout_mode=layout_mode,
+                                                        scale_format=scale_format)
+        grad_gate_up_q = quantize_grouped_wgrad_operand_128x1(grad_gate_up_grouped, meta, layout_mode=layout_mode,
+                                                        scale_format=scale_format)
+        x_q = quantize_grouped_wgrad_operand_128x1(x_grouped, meta, layout_mode=layout_mode,
+                                                        scale_format=scale_format)
     else:
         grad_y_q = hidden_q = grad_gate_up_q = x_q = None
 

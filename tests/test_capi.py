@@ -44,10 +44,11 @@ def test_struct_layout_matches_header():
     assert ctypes.sizeof(_lib.Sm100WgradArgs) == 8 * 8 + 8 * 7 + 4 * 4 + 0
     assert _lib.Sm100WgradArgs.max_ctas.offset == ctypes.sizeof(_lib.Sm100WgradArgs) - 4
     assert ctypes.sizeof(_lib.Sm100WgradMetaOut) == 14 * 8
-    # Sm100WgradQuantArgs: 17 eight-byte slots (int32 fields padded to 8)
-    assert ctypes.sizeof(_lib.Sm100WgradQuantArgs) == 17 * 8
+    # Sm100WgradQuantArgs: 18 eight-byte slots (int32 fields padded to 8)
+    assert ctypes.sizeof(_lib.Sm100WgradQuantArgs) == 18 * 8
     assert _lib.Sm100WgradQuantArgs.block_rows.offset == 15 * 8
     assert _lib.Sm100WgradQuantArgs.x_rows.offset == 16 * 8
+    assert _lib.Sm100WgradQuantArgs.scale_format.offset == 17 * 8
 
 
 def test_invalid_arguments_rejected_without_gpu():
