@@ -70,6 +70,11 @@ extern "C" {
  * A scale with mantissa bits set is taken as 1.0 and sets device error 6.
  * Never chosen by AUTO. */
 #define SM100_WGRAD_TILE_128x192_UE8M0 7
+/* 256x256 tile over a pair of CTAs (a cluster of two on neighbouring SMs):
+ * tcgen05.mma cta_group::2 with each CTA loading its 128 rows of lhs and half
+ * of the rhs tile, 8 promotion warps per CTA. */
+#define SM100_WGRAD_TILE_256x256_PAIR 8
+#define SM100_WGRAD_TILE_256x256_PAIR_W16 9   /* the same with 16 promotion warps per CTA */
 
 typedef struct Sm100WgradArgs {
   const void* lhs_data;      /* FP8 e4m3 [M][lhs_pitch]                              */

@@ -116,7 +116,8 @@ int pick_bn(int32_t tile_config, int64_t n) {
   if (tile_config == SM100_WGRAD_TILE_128x128 || tile_config == SM100_WGRAD_TILE_128x128_2CTA) return 128;
   if (tile_config == SM100_WGRAD_TILE_128x192_W12 || tile_config == SM100_WGRAD_TILE_128x192_UE8M0) return 192;
   if (tile_config == SM100_WGRAD_TILE_128x256 || tile_config == SM100_WGRAD_TILE_128x256_W8 ||
-      tile_config == SM100_WGRAD_TILE_128x256_W16)
+      tile_config == SM100_WGRAD_TILE_128x256_W16 || tile_config == SM100_WGRAD_TILE_256x256_PAIR ||
+      tile_config == SM100_WGRAD_TILE_256x256_PAIR_W16)
     return 256;
   // auto: the wide tile halves operand re-reads per output byte; a narrow N
   // would only fill it with zero columns.
@@ -131,8 +132,8 @@ constexpr int64_t kShortKBlocksPerExpert = 2;
 int pick_epi_warps(int32_t tile_config, int bn, int64_t total_blocks, int64_t num_experts) {
   if (tile_config == SM100_WGRAD_TILE_128x128_2CTA) return 4;
   if (tile_config == SM100_WGRAD_TILE_128x192_W12 || tile_config == SM100_WGRAD_TILE_128x192_UE8M0) return 12;
-  if (bn != 256 || tile_config == SM100_WGRAD_TILE_128x256_W8) return 8;
-  if (tile_config == SM100_WGRAD_TILE_128x256_W16) return 16;
+  if (bn != 256 || tile_config == SM100_WGRAD_TILE_128x256_W8 || tile_config == SM100_WGRAD_TILE_256x256_PAIR) return 8;
+  if (tile_config == SM100_WGRAD_TILE_128x256_W16 || tile_config == SM100_WGRAD_TILE_256x256_PAIR_W16) return 16;
   return total_blocks <= kShortKBlocksPerExpert * num_experts ? 16 : 8;
 }
 
@@ -161,7 +162,7 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   if (a->num_experts < 0 || a->m <= 0 || a->n <= 0 || a->k_rows < 0 || a->total_blocks < 0)
     return SM100_WGRAD_ERR_INVALID_ARG;
   if (a->out_dtype != SM100_WGRAD_OUT_BF16 && a->out_dtype != SM100_WGRAD_OUT_F32) return SM100_WGRAD_ERR_INVALID_ARG;
-  if (a->tile_config < SM100_WGRAD_TILE_AUTO || a->tile_config > SM100_WGRAD_TILE_128x192_UE8M0)
+  if (a->tile_config < SM100_WGRAD_TILE_AUTO || a->tile_config > SM100_WGRAD_TILE_256x256_PAIR_W16)
     return SM100_WGRAD_ERR_INVALID_ARG;
   // TMA: output row pitch and scale-vector chunks must be 16-byte multiples.
   if (a->m % 16 != 0 || a->n % 16 != 0) return SM100_WGRAD_ERR_UNSUPPORTED;
@@ -184,11 +185,15 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   if (st != SM100_WGRAD_OK) return st;
 
   const int bn = pick_bn(a->tile_config, a->n);
+  const bool pair =
+      a->tile_config == SM100_WGRAD_TILE_256x256_PAIR || a->tile_config == SM100_WGRAD_TILE_256x256_PAIR_W16;
+  const int bm = pair ? 256 : 128;
   CUtensorMap ta{}, tb{}, to{};
   if (has_operands) {
     st = encode_operand_map(&ta, a->lhs_data, a->k_rows, a->m, a->lhs_pitch, 128);
     if (st != SM100_WGRAD_OK) return st;
-    st = encode_operand_map(&tb, a->rhs_data, a->k_rows, a->n, a->rhs_pitch, bn);
+    // a pair CTA loads half of the rhs tile's rows
+    st = encode_operand_map(&tb, a->rhs_data, a->k_rows, a->n, a->rhs_pitch, pair ? bn / 2 : bn);
     if (st != SM100_WGRAD_OK) return st;
   }
   st = encode_out_map(&to, a->out, a->out_dtype == SM100_WGRAD_OUT_F32, a->num_experts, a->m, a->n);
@@ -205,8 +210,9 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   p.m = static_cast<int>(a->m);
   p.n = static_cast<int>(a->n);
   p.bn = bn;
+  p.bm = bm;
   p.tiles_n = static_cast<int>((a->n + bn - 1) / bn);
-  const int64_t tiles_m = (a->m + 127) / 128;
+  const int64_t tiles_m = (a->m + bm - 1) / bm;
   const int64_t tpe = tiles_m * p.tiles_n;
   const int64_t num_tiles = tpe * a->num_experts;
   if (num_tiles > INT32_MAX) return SM100_WGRAD_ERR_UNSUPPORTED;
@@ -231,13 +237,21 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   p.ue8m0 = a->tile_config == SM100_WGRAD_TILE_128x192_UE8M0 ? 1 : 0;
   // The known-answer modes instrument the promotion loop, which the UE8M0 kernel does not have.
   if (p.ue8m0 && p.mode != wgrad::kModeNormal) return SM100_WGRAD_ERR_UNSUPPORTED;
+  if (pair && p.mode != wgrad::kModeNormal) return SM100_WGRAD_ERR_UNSUPPORTED;
   // Test-only failure injection of the bounded-wait path (never set in normal use).
   const char* inject = std::getenv("SM100_WGRAD_DEBUG_INJECT");
   p.inject = (inject != nullptr && std::strcmp(inject, "withhold_first_load") == 0) ? wgrad::kInjectWithholdFirstLoad : 0;
 
   int grid = info.sm_count * (p.epi_warps == 4 ? 2 : 1);  // the 4-warp tile runs two CTAs per SM
   if (a->max_ctas > 0 && a->max_ctas < grid) grid = a->max_ctas;
-  if (num_tiles < grid) grid = static_cast<int>(num_tiles);
+  if (pair) {
+    // one cluster of two CTAs per tile at most; whole clusters only
+    if (2 * num_tiles < grid) grid = static_cast<int>(2 * num_tiles);
+    grid &= ~1;
+    if (grid < 2) grid = 2;
+  } else if (num_tiles < grid) {
+    grid = static_cast<int>(num_tiles);
+  }
   const cudaError_t err = wgrad::launch_grouped_wgrad(ta, tb, to, p, grid, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? SM100_WGRAD_OK : SM100_WGRAD_ERR_LAUNCH;
 }

@@ -68,9 +68,14 @@ __device__ unsigned long long g_wgrad_prof[kProfSlots];
 #define WGRAD_PROF_INC(slot) ((void)0)
 #endif
 #if WGRAD_PROFILE
-#define WGRAD_PROF_PTR s_prof
+#define WGRAD_PROF_PTR s_prof, s_issue
+#define WGRAD_PROF_LATENCY(stage)                                                                   \
+  do {                                                                                           \
+    if (prof_lane) s_prof[kProfLoadLatency] += static_cast<unsigned long long>(clock64() - s_issue[stage]); \
+  } while (0)
 #else
-#define WGRAD_PROF_PTR nullptr
+#define WGRAD_PROF_PTR nullptr, nullptr
+#define WGRAD_PROF_LATENCY(stage) ((void)0)
 #endif
 
 namespace {
@@ -93,17 +98,19 @@ constexpr int FIRST_EPI_WARP = 4;
 // promotion warps take the rest: 16 warps: 640 x 96 = 128 x 32 + 512 x 112;
 // 8 warps: 384 x 168 >= 128 x 56 + 256 x 224; 4 warps, 2 CTAs: 256 x 128 =
 // 128 x 56 + 128 x 200.
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR = false>
 struct Cfg {
   static constexpr int EPI_WARPS = EPI;
   static constexpr int THREADS = 32 * (4 + EPI_WARPS);
   static constexpr int CTAS_PER_SM = EPI_WARPS == 4 ? 2 : 1;
-  static constexpr int STAGES = EPI_WARPS == 4 ? 2 : 3;
+  // A pair CTA holds half of B, so a stage is 32 KB instead of 48 KB.
+  static constexpr int STAGES = PAIR ? 4 : (EPI_WARPS == 4 ? 2 : 3);
   static constexpr uint32_t REGS_CONTROL = EPI_WARPS == 16 ? 32 : (EPI_WARPS == 12 ? 40 : 56);
   static constexpr uint32_t REGS_EPILOGUE =
       EPI_WARPS == 16 ? 112 : (EPI_WARPS == 12 ? 152 : (EPI_WARPS == 4 ? 200 : 224));
   static constexpr int A_BYTES = BM * BK;
-  static constexpr int B_BYTES = BN * BK;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows of B this CTA loads
+  static constexpr int B_BYTES = B_ROWS * BK;
   static constexpr int SCALE_FLOATS = BM + BN;
   static constexpr int COLS_PER_WARP = BN / (EPI_WARPS / 4);  // EPI_WARPS / 4 column groups
   // tcgen05.ld columns per load: 32 when two such buffers fit beside the accumulator
@@ -145,26 +152,38 @@ struct TileCoord {
   int e, m0, n0;
 };
 
-__device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, int tile) {
+// Tile -> (expert, first row of this CTA, first column). p.bm is the tile's M
+// (256 for a CTA pair, whose odd CTA starts row_off = 128 rows further).
+__device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, int tile, int row_off = 0) {
   const int e_slot = tile / p.tiles_per_expert;
   const int local = tile - e_slot * p.tiles_per_expert;
   const int tm = local / p.tiles_n;
   const int tn = local - tm * p.tiles_n;
   TileCoord c;
   c.e = p.expert_order != nullptr ? __ldg(p.expert_order + e_slot) : e_slot;
-  c.m0 = tm * BM;
+  c.m0 = tm * p.bm + row_off;
   c.n0 = tn * p.bn;
   return c;
 }
 
 // TMA producer (one thread): for every K block of every tile this CTA owns,
 // the A and B operand tiles into the STAGES-deep ring and the block's A / B
-// scale vectors into the SCALE_STAGES-deep scale ring.
-template <class C, int BN>
+// scale vectors into the SCALE_STAGES-deep scale ring. In a CTA pair (PAIR)
+// each CTA loads its own 128 rows of A and its half of B's rows, and both
+// loads complete on the even CTA's full barrier, whose producer announces the
+// bytes of both; at the end each producer waits until the MMA has released
+// every stage it filled, so no release arrives after this CTA has exited.
+template <class C, int BN, bool PAIR = false>
 __device__ __forceinline__ void run_producer(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GemmParams& p,
                                              uint8_t* s_a, uint8_t* s_b, float* s_scale, uint64_t* full_bar,
                                              uint64_t* empty_bar, uint64_t* sfull_bar, uint64_t* sempty_bar,
-                                             volatile int* abort_flag, unsigned long long* s_prof) {
+                                             volatile int* abort_flag, unsigned long long* s_prof,
+                                             long long* issue_clock, int tile_begin = -1, int tile_stride = 0,
+                                             uint32_t rank = 0) {
+  if (tile_begin < 0) {
+    tile_begin = blockIdx.x;
+    tile_stride = gridDim.x;
+  }
 #if WGRAD_PROFILE
   const bool prof_lane = true;  // called by the producer lane only
 #else
@@ -172,26 +191,39 @@ __device__ __forceinline__ void run_producer(const CUtensorMap& tmap_a, const CU
 #endif
   int stage = 0, sstage = 0;
   uint32_t phase = 0, sphase = 0;
-  for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-    const TileCoord tc = decode_tile(p, tile);
+  bool ok = true;
+  for (int tile = tile_begin; tile < p.num_tiles && ok; tile += tile_stride) {
+    const TileCoord tc = decode_tile(p, tile, static_cast<int>(rank) * BM);
     const int kb0 = __ldg(p.block_offsets + tc.e);
     const int nkb = __ldg(p.block_offsets + tc.e + 1) - kb0;
     const int krow0 = __ldg(p.k_row_offsets + tc.e);
-    const uint32_t a_scale_bytes = static_cast<uint32_t>(min(BM, p.m - tc.m0)) * 4u;
+    // the odd CTA of a pair may lie wholly below the last row of M
+    const uint32_t a_scale_bytes = static_cast<uint32_t>(max(0, min(BM, p.m - tc.m0))) * 4u;
     const uint32_t b_scale_bytes = static_cast<uint32_t>(min(BN, p.n - tc.n0)) * 4u;
-    bool ok = true;
     for (int kb = 0; kb < nkb && ok; ++kb) {
       WGRAD_PROF_T(tw0);
       ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, kDevTimeoutProducer);
       WGRAD_PROF_ADD(kProfProducerWaitStage, tw0);
       if (!ok) break;
-      mbar_arrive_expect_tx(&full_bar[stage], C::A_BYTES + C::B_BYTES);
+      if (issue_clock != nullptr) issue_clock[stage] = clock64();  // profile builds only
       // Test-only failure injection: announce the first stage's bytes but
       // issue no copy, so the stage never fills and the bounded waits of
       // the consumers expire (device error word, clean exit).
-      if (!(p.inject == kInjectWithholdFirstLoad && tile == static_cast<int>(blockIdx.x) && kb == 0)) {
-        tma_load_2d(s_a + stage * C::A_BYTES, &tmap_a, &full_bar[stage], krow0 + kb * BK, tc.m0);
-        tma_load_2d(s_b + stage * C::B_BYTES, &tmap_b, &full_bar[stage], krow0 + kb * BK, tc.n0);
+      const bool withhold = p.inject == kInjectWithholdFirstLoad && tile == tile_begin && kb == 0;
+      if constexpr (PAIR) {
+        const uint32_t leader_full = cluster_addr(&full_bar[stage], 0);
+        if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * (C::A_BYTES + C::B_BYTES));
+        if (!withhold) {
+          tma_load_2d_pair(s_a + stage * C::A_BYTES, &tmap_a, leader_full, krow0 + kb * BK, tc.m0);
+          tma_load_2d_pair(s_b + stage * C::B_BYTES, &tmap_b, leader_full, krow0 + kb * BK,
+                           tc.n0 + static_cast<int>(rank) * C::B_ROWS);
+        }
+      } else {
+        mbar_arrive_expect_tx(&full_bar[stage], C::A_BYTES + C::B_BYTES);
+        if (!withhold) {
+          tma_load_2d(s_a + stage * C::A_BYTES, &tmap_a, &full_bar[stage], krow0 + kb * BK, tc.m0);
+          tma_load_2d(s_b + stage * C::B_BYTES, &tmap_b, &full_bar[stage], krow0 + kb * BK, tc.n0);
+        }
       }
       if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
 
@@ -202,11 +234,17 @@ __device__ __forceinline__ void run_producer(const CUtensorMap& tmap_a, const CU
       float* dst = s_scale + sstage * C::SCALE_FLOATS;
       const size_t blk = static_cast<size_t>(kb0 + kb);
       mbar_arrive_expect_tx(&sfull_bar[sstage], a_scale_bytes + b_scale_bytes);
-      bulk_load_1d(dst, p.sa + blk * p.m + tc.m0, a_scale_bytes, &sfull_bar[sstage]);
+      if (a_scale_bytes > 0) bulk_load_1d(dst, p.sa + blk * p.m + tc.m0, a_scale_bytes, &sfull_bar[sstage]);
       bulk_load_1d(dst + BM, p.sb + blk * p.n + tc.n0, b_scale_bytes, &sfull_bar[sstage]);
       if (++sstage == SCALE_STAGES) { sstage = 0; sphase ^= 1u; }
     }
-    if (!ok) break;
+  }
+  if constexpr (PAIR) {
+    // Drain: every stage filled so far has been released by the MMA.
+    for (int i = 0; i < C::STAGES && ok; ++i) {
+      ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, kDevTimeoutProducer);
+      if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+    }
   }
 }
 
@@ -345,11 +383,16 @@ __device__ __forceinline__ bool store_warp_tile(float (&fin)[COLS], const CUtens
   return ok;
 }
 
-template <int BN, int EPI>
-__global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_SM)
+// PAIR: a cluster of two CTAs computes a 256 x BN tile with cta_group::2
+// UMMAs issued by the even CTA; each CTA loads its 128 rows of A and half of
+// B (a third less operand traffic per SM than a 128 x BN tile) and promotes
+// its own 128 TMEM lanes. The odd CTA's promotion warps release a partial on
+// the even CTA's barrier.
+template <int BN, int EPI, bool PAIR>
+__global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR>::CTAS_PER_SM)
     grouped_wgrad_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                          const __grid_constant__ CUtensorMap tmap_out, const GemmParams p) {
-  using C = Cfg<BN, EPI>;
+  using C = Cfg<BN, EPI, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
@@ -369,8 +412,13 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int tile_begin = PAIR ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
+  const int tile_stride = PAIR ? static_cast<int>(cluster_count_x()) : static_cast<int>(gridDim.x);
+  const int row_off = static_cast<int>(rank) * BM;
 #if WGRAD_PROFILE
   __shared__ unsigned long long s_prof[kProfSlots];
+  __shared__ long long s_issue[8];
   const bool prof_lane = lane == 0 && (warp == 0 || warp == 1 || warp == FIRST_EPI_WARP);
   if (threadIdx.x < kProfSlots) s_prof[threadIdx.x] = threadIdx.x == kProfCtas ? 1ull : 0ull;
 #endif
@@ -386,7 +434,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull_bar[i], 1);
-      mbar_init(&tempty_bar[i], C::EPI_WARPS);
+      mbar_init(&tempty_bar[i], (PAIR ? 2 : 1) * C::EPI_WARPS);  // a pair's even CTA hears both CTAs
     }
     for (int i = 0; i < C::EPI_WARPS; ++i) mbar_init(&oldout_bar[i], 1);
     *abort_flag = 0;
@@ -398,11 +446,17 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
     tma_prefetch_desc(&tmap_out);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_holder, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
@@ -410,15 +464,16 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) run_producer<C, BN>(tmap_a, tmap_b, p, s_a, s_b, s_scale, full_bar, empty_bar, sfull_bar, sempty_bar,
-                                       abort_flag, WGRAD_PROF_PTR);
-  } else if (warp == 1) {
+    if (lane == 0)
+      run_producer<C, BN, PAIR>(tmap_a, tmap_b, p, s_a, s_b, s_scale, full_bar, empty_bar, sfull_bar, sempty_bar,
+                                abort_flag, WGRAD_PROF_PTR, tile_begin, tile_stride, rank);
+  } else if (warp == 1 && rank == 0) {
     // ------------------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc = umma_idesc_e4m3_f32(BM, BN);
+    constexpr uint32_t idesc = umma_idesc_e4m3_f32(PAIR ? 2 * BM : BM, BN);
     int stage = 0, acc = 0;
     uint32_t phase = 0, aphase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+    for (int tile = tile_begin; tile < p.num_tiles && ok; tile += tile_stride) {
       const TileCoord tc = decode_tile(p, tile);
       const int nkb = __ldg(p.block_offsets + tc.e + 1) - __ldg(p.block_offsets + tc.e);
       // K slices of 32 rows in the expert's last block: 4 in the padded layout;
@@ -432,6 +487,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
         WGRAD_PROF_T(tm0);
         ok = mbar_wait2(&tempty_bar[acc], aphase ^ 1u, &full_bar[stage], phase, abort_flag, kDevTimeoutMma);
         WGRAD_PROF_ADD(kProfMmaWait, tm0);
+        WGRAD_PROF_LATENCY(stage);
         WGRAD_PROF_T(tm1);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
@@ -444,11 +500,23 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
           for (int k = 0; k < BK / 32; ++k) {
             if (k >= atoms) break;
             // advance 32 bytes (one K=32 FP8 slice) inside the 128-byte swizzle atom
-            umma_f8(d_tmem, umma_desc_k_sw128(a_addr + k * 32), umma_desc_k_sw128(b_addr + k * 32), idesc,
-                    k > 0 ? 1u : 0u);
+            if constexpr (PAIR) {
+              umma_f8_pair(d_tmem, umma_desc_k_sw128(a_addr + k * 32), umma_desc_k_sw128(b_addr + k * 32), idesc,
+                           k > 0 ? 1u : 0u);
+            } else {
+              umma_f8(d_tmem, umma_desc_k_sw128(a_addr + k * 32), umma_desc_k_sw128(b_addr + k * 32), idesc,
+                      k > 0 ? 1u : 0u);
+            }
           }
-          umma_commit(&empty_bar[stage]);
-          umma_commit(&tfull_bar[acc]);
+          if constexpr (PAIR) {  // release the stage and publish the partial in both CTAs
+            umma_commit_pair(cluster_addr(&empty_bar[stage], 0));
+            umma_commit_pair(cluster_addr(&empty_bar[stage], 1));
+            umma_commit_pair(cluster_addr(&tfull_bar[acc], 0));
+            umma_commit_pair(cluster_addr(&tfull_bar[acc], 1));
+          } else {
+            umma_commit(&empty_bar[stage]);
+            umma_commit(&tfull_bar[acc]);
+          }
         }
         __syncwarp();
         WGRAD_PROF_ADD(kProfMmaIssue, tm1);
@@ -470,8 +538,10 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
     int acc = 0, sstage = 0;
     uint32_t aphase = 0, sphase = 0, oldout_phase = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-      const TileCoord tc = decode_tile(p, tile);
+    // the partial's release goes to the pair's even CTA
+    const uint32_t tempty_addr0 = PAIR ? cluster_addr(&tempty_bar[0], 0) : 0u;
+    for (int tile = tile_begin; tile < p.num_tiles && ok; tile += tile_stride) {
+      const TileCoord tc = decode_tile(p, tile, row_off);
       const int nkb = __ldg(p.block_offsets + tc.e + 1) - __ldg(p.block_offsets + tc.e);
       float fin[C::COLS_PER_WARP];
 #pragma unroll
@@ -509,7 +579,10 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
           } else {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+            if (lane == 0) {
+              if (PAIR && rank != 0) mbar_arrive_cluster(tempty_addr0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
+              else mbar_arrive(&tempty_bar[acc]);
+            }
           }
 #pragma unroll
           for (int j = 0; j < CH; j += 4) {
@@ -572,12 +645,14 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // no cross-CTA arrival or UMMA is left in flight
 #if WGRAD_PROFILE
   if (threadIdx.x < kProfSlots) atomicAdd(&g_wgrad_prof[threadIdx.x], s_prof[threadIdx.x]);
 #endif
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -590,22 +665,21 @@ __global__ void __launch_bounds__(Cfg<BN, EPI>::THREADS, Cfg<BN, EPI>::CTAS_PER_
 // sum_b sum_k qa qb sa sb, rounded once per UMMA instead of once per K block.
 //
 // Warps: 0 TMA producer (shared with the promotion kernel), 1 MMA issuer,
-// 4..7 scale-factor writers, 8..19 epilogue (three 64-column warps per TMEM
-// lane quarter). TMEM: two 192-column accumulators, then SF_STAGES
-// scale-factor stages of 16 columns (A: 4 columns, B: 8 columns from +4).
-// Scale-factor layout in TMEM (one 32-bit word per lane and column, the
-// layout tcgen05.cp 32x128b.warpx4 writes from the CUTLASS Sm1xx block-scaled
-// atom): row r of A or B sits in lane r % 32, column r / 32, and byte j of the
-// word is the scale of K slice j; every lane quarter holds the same copy.
-// Each writer warp fills its own lane quarter with tcgen05.st. The four K
-// slices of a 128-row block share one scale, so all four bytes are equal and
-// the byte selectors of the instruction descriptor stay 0.
+// 2 scale-factor writer, 4..15 epilogue (three 64-column warps per TMEM lane
+// quarter). Per K block the writer turns the block's fp32 scales into E8M0
+// bytes in shared memory, in the 32-row x 16-byte layout of the CUTLASS Sm1xx
+// block-scaled atom: row r of A or B at byte 16 (r % 32) + 4 (r / 32 % 4) + j
+// of its 128-row group, j the K slice. The MMA thread copies them into TMEM
+// with tcgen05.cp 32x128b.warpx4 (row r -> lane r % 32 of every quarter,
+// column r / 32), in order with its UMMAs. TMEM: two 192-column accumulators,
+// then SF_STAGES scale-factor stages of 16 columns (A: 4, B: 8 from +4). The
+// four K slices of a 128-row block share one scale, so all four bytes of a
+// word are equal and the instruction's byte selectors stay 0.
 struct BsCfg {
   static constexpr int BN = 192;
   static constexpr int STAGES = 4;
-  static constexpr int FIRST_SF_WARP = 4;
-  static constexpr int SF_WARPS = 4;
-  static constexpr int FIRST_EPI = 8;
+  static constexpr int SF_WARP = 2;
+  static constexpr int FIRST_EPI = 4;
   static constexpr int EPI_WARPS = 12;
   static constexpr int THREADS = 32 * (FIRST_EPI + EPI_WARPS);
   static constexpr int COLS_PER_WARP = BN / (EPI_WARPS / 4);  // 64
@@ -614,20 +688,24 @@ struct BsCfg {
   static constexpr int SCALE_FLOATS = BM + BN;
   static constexpr int OUT_STAGE_BYTES_PER_WARP = 4096;
   static constexpr int SF_STAGES = 4;
+  static constexpr int SF_A_BYTES = 512;    // 128 rows
+  static constexpr int SF_B_BYTES = 1024;   // 256 rows (BN = 192 uses 6 of the 8 columns)
+  static constexpr int SF_STAGE_BYTES = SF_A_BYTES + SF_B_BYTES;
   static constexpr int SF_COL0 = 2 * BN;
   static constexpr int SF_STAGE_COLS = 16;
   static constexpr int SF_B_OFFSET = 4;
   static constexpr int TMEM_COLS = 512;
   static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + EPI_WARPS * OUT_STAGE_BYTES_PER_WARP +
-                                    SCALE_STAGES * SCALE_FLOATS * 4 + 512 /*barriers*/ + 1024 /*align*/;
+                                    SF_STAGES * SF_STAGE_BYTES + SCALE_STAGES * SCALE_FLOATS * 4 +
+                                    512 /*barriers*/ + 1024 /*align*/;
   static_assert(SF_COL0 + SF_STAGES * SF_STAGE_COLS <= TMEM_COLS, "TMEM columns");
   static_assert(COLS_PER_WARP * 32 * 2 == OUT_STAGE_BYTES_PER_WARP, "one BF16 staging round per tile");
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
 // E8M0 byte of a positive power-of-two fp32 scale, replicated into the four
-// bytes of a TMEM word. Anything else (mantissa bits, zero, subnormal, inf,
-// NaN, negative) sets device error 6 and encodes as 1.0.
+// bytes of a word. Anything else (mantissa bits, zero, subnormal, inf, NaN,
+// negative) sets device error 6 and encodes as 1.0.
 __device__ __forceinline__ uint32_t e8m0_word(float s) {
   const uint32_t bits = __float_as_uint(s);
   const uint32_t e = bits >> 23;  // sign bit set -> e > 255
@@ -648,14 +726,15 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
   uint8_t* s_a = smem;
   uint8_t* s_b = s_a + C::STAGES * C::A_BYTES;
   uint8_t* s_out = s_b + C::STAGES * C::B_BYTES;
-  float* s_scale = reinterpret_cast<float*>(s_out + C::EPI_WARPS * C::OUT_STAGE_BYTES_PER_WARP);
+  uint8_t* s_sf = s_out + C::EPI_WARPS * C::OUT_STAGE_BYTES_PER_WARP;    // [SF_STAGES][A 512 | B 1024]
+  float* s_scale = reinterpret_cast<float*>(s_sf + C::SF_STAGES * C::SF_STAGE_BYTES);
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_scale + SCALE_STAGES * C::SCALE_FLOATS);
   uint64_t* full_bar = bars;                             // [STAGES]      TMA -> MMA
   uint64_t* empty_bar = full_bar + C::STAGES;            // [STAGES]      MMA -> TMA
-  uint64_t* sfull_bar = empty_bar + C::STAGES;           // [SCALE_STAGES] TMA -> SF writers
-  uint64_t* sempty_bar = sfull_bar + SCALE_STAGES;       // [SCALE_STAGES] SF writers -> TMA
-  uint64_t* sffull_bar = sempty_bar + SCALE_STAGES;      // [SF_STAGES]   SF writers -> MMA
-  uint64_t* sfempty_bar = sffull_bar + C::SF_STAGES;     // [SF_STAGES]   MMA -> SF writers
+  uint64_t* sfull_bar = empty_bar + C::STAGES;           // [SCALE_STAGES] TMA -> SF writer
+  uint64_t* sempty_bar = sfull_bar + SCALE_STAGES;       // [SCALE_STAGES] SF writer -> TMA
+  uint64_t* sffull_bar = sempty_bar + SCALE_STAGES;      // [SF_STAGES]   SF writer -> MMA
+  uint64_t* sfempty_bar = sffull_bar + C::SF_STAGES;     // [SF_STAGES]   MMA (copies done) -> SF writer
   uint64_t* tfull_bar = sfempty_bar + C::SF_STAGES;      // [2] MMA -> epilogue
   uint64_t* tempty_bar = tfull_bar + 2;                  // [2] epilogue -> MMA
   uint64_t* oldout_bar = tempty_bar + 2;                 // [EPI_WARPS] previous output (accumulate)
@@ -664,6 +743,15 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+#if WGRAD_PROFILE
+  // Slots as the promotion kernel: MmaWait = operand + scale-factor stage,
+  // EpiWait / EpiPromote = scale-factor writer wait / work, EpiStoreWait =
+  // epilogue wait for the accumulator, EpiStore = its drain + store.
+  __shared__ unsigned long long s_prof[kProfSlots];
+  __shared__ long long s_issue[8];
+  const bool prof_lane = lane == 0 && (warp == 0 || warp == 1 || warp == BsCfg::SF_WARP || warp == BsCfg::FIRST_EPI);
+  if (threadIdx.x < kProfSlots) s_prof[threadIdx.x] = threadIdx.x == kProfCtas ? 1ull : 0ull;
+#endif
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::STAGES; ++i) {
@@ -672,10 +760,10 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
     }
     for (int i = 0; i < SCALE_STAGES; ++i) {
       mbar_init(&sfull_bar[i], 1);
-      mbar_init(&sempty_bar[i], C::SF_WARPS);
+      mbar_init(&sempty_bar[i], 1);
     }
     for (int i = 0; i < C::SF_STAGES; ++i) {
-      mbar_init(&sffull_bar[i], C::SF_WARPS);
+      mbar_init(&sffull_bar[i], 1);
       mbar_init(&sfempty_bar[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -703,7 +791,7 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) run_producer<C, BN>(tmap_a, tmap_b, p, s_a, s_b, s_scale, full_bar, empty_bar, sfull_bar, sempty_bar,
-                                       abort_flag, nullptr);
+                                       abort_flag, WGRAD_PROF_PTR);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc = umma_idesc_mxf8_e4m3_ue8m0(BM, BN);
@@ -723,14 +811,22 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
       for (int kb = 0; kb < nkb; ++kb) {
         const int atoms = kb + 1 == nkb ? last_atoms : BK / 32;
+        WGRAD_PROF_T(tm0);
         ok = mbar_wait2(&full_bar[stage], phase, &sffull_bar[sfs], sfphase, abort_flag, kDevTimeoutMma);
+        WGRAD_PROF_ADD(kProfMmaWait, tm0);
+        WGRAD_PROF_LATENCY(stage);
+        WGRAD_PROF_T(tm1);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
         if (lane == 0) {
           const uint32_t a_addr = smem_u32(s_a + stage * C::A_BYTES);
           const uint32_t b_addr = smem_u32(s_b + stage * C::B_BYTES);
+          const uint32_t sf_smem = smem_u32(s_sf + sfs * C::SF_STAGE_BYTES);
           const uint32_t sfa = tmem_base + static_cast<uint32_t>(C::SF_COL0 + sfs * C::SF_STAGE_COLS);
+          tmem_cp_32x128b_warpx4(sfa, smem_desc_rows16(sf_smem));
+          tmem_cp_32x128b_warpx4(sfa + C::SF_B_OFFSET, smem_desc_rows16(sf_smem + C::SF_A_BYTES));
+          tmem_cp_32x128b_warpx4(sfa + C::SF_B_OFFSET + 4, smem_desc_rows16(sf_smem + C::SF_A_BYTES + 512));
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k) {
             if (k >= atoms) break;
@@ -741,6 +837,7 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
           umma_commit(&sfempty_bar[sfs]);
         }
         __syncwarp();
+        WGRAD_PROF_ADD(kProfMmaIssue, tm1);
         if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         if (++sfs == C::SF_STAGES) { sfs = 0; sfphase ^= 1u; }
       }
@@ -750,10 +847,8 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
       acc ^= 1;
       if (acc == 0) aphase ^= 1u;
     }
-  } else if (warp >= C::FIRST_SF_WARP && warp < C::FIRST_EPI) {
-    // ------------------------------------------------------------ scale-factor writers
-    const int quarter = warp & 3;
-    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+  } else if (warp == C::SF_WARP) {
+    // ------------------------------------------------------------ scale-factor writer
     int sstage = 0, sfs = 0;
     uint32_t sphase = 0, sfphase = 0;
     bool ok = true;
@@ -763,32 +858,39 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
       const int a_valid = min(BM, p.m - tc.m0);
       const int b_valid = min(BN, p.n - tc.n0);
       for (int kb = 0; kb < nkb; ++kb) {
+        WGRAD_PROF_T(tf0);
         ok = mbar_wait2(&sfull_bar[sstage], sphase, &sfempty_bar[sfs], sfphase ^ 1u, abort_flag, kDevTimeoutEpilogue);
+        WGRAD_PROF_ADD(kProfEpiWait, tf0);
+        WGRAD_PROF_T(tf1);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
-        tc_fence_after();
         const float* sc = s_scale + sstage * C::SCALE_FLOATS;
-        uint32_t wa[4], wb[8];
+        uint32_t w[12];  // A rows lane + 32 c (c < 4), then B rows lane + 32 (c - 4)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int r = lane + 32 * c;
-          wa[c] = r < a_valid ? e8m0_word(sc[r]) : 127u * 0x01010101u;
+          w[c] = r < a_valid ? e8m0_word(sc[r]) : 127u * 0x01010101u;
         }
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const int r = lane + 32 * c;
-          wb[c] = (r < BN && r < b_valid) ? e8m0_word(sc[BM + r]) : 127u * 0x01010101u;
+          w[4 + c] = (r < BN && r < b_valid) ? e8m0_word(sc[BM + r]) : 127u * 0x01010101u;
         }
-        const uint32_t t = tmem_base + lane_addr + static_cast<uint32_t>(C::SF_COL0 + sfs * C::SF_STAGE_COLS);
-        tmem_st_32x32b_x4(t, wa[0], wa[1], wa[2], wa[3]);
-        tmem_st_32x32b_x8(t + C::SF_B_OFFSET, wb);
-        tmem_wait_st();
-        tc_fence_before();
+        const uint32_t dst = smem_u32(s_sf + sfs * C::SF_STAGE_BYTES) + lane * 16;
+        st_shared_v4(dst, w[0], w[1], w[2], w[3]);
+        st_shared_v4(dst + C::SF_A_BYTES, w[4], w[5], w[6], w[7]);
+        st_shared_v4(dst + C::SF_A_BYTES + 512, w[8], w[9], w[10], w[11]);
+        WGRAD_PROF_ADD(kProfSfConvert, tf1);
+        WGRAD_PROF_T(tf2);
+        fence_proxy_async_smem();  // the copies read through the async proxy
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&sempty_bar[sstage]);
           mbar_arrive(&sffull_bar[sfs]);
         }
+        WGRAD_PROF_ADD(kProfSfPublish, tf2);
+        WGRAD_PROF_ADD(kProfEpiPromote, tf1);
+        WGRAD_PROF_INC(kProfKBlocks);
         if (++sstage == SCALE_STAGES) { sstage = 0; sphase ^= 1u; }
         if (++sfs == C::SF_STAGES) { sfs = 0; sfphase ^= 1u; }
       }
@@ -811,7 +913,9 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
 #pragma unroll
         for (int j = 0; j < C::COLS_PER_WARP; ++j) fin[j] = 0.f;
       } else {
+        WGRAD_PROF_T(te0);
         ok = mbar_wait(&tfull_bar[acc], aphase, abort_flag, kDevTimeoutEpilogue);
+        WGRAD_PROF_ADD(kProfEpiStoreWait, te0);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
@@ -834,11 +938,14 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
         if (acc == 0) aphase ^= 1u;
       }
       const int col0 = tc.n0 + cgroup * C::COLS_PER_WARP;
+      WGRAD_PROF_T(ts0);
+      WGRAD_PROF_INC(kProfTiles);
       // The previous tile's TMA store must have finished reading the staging buffer.
       if (lane == 0) bulk_wait_group_read0();
       __syncwarp();
       ok = store_warp_tile<C::COLS_PER_WARP, C::OUT_STAGE_BYTES_PER_WARP>(
           fin, tmap_out, p, tc, quarter, lane, col0, stage_out, &oldout_bar[ew], oldout_phase, abort_flag);
+      WGRAD_PROF_ADD(kProfEpiStore, ts0);
     }
     if (lane == 0) bulk_wait_group0();  // all output writes complete before exit
     __syncwarp();
@@ -846,6 +953,9 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+#if WGRAD_PROFILE
+  if (threadIdx.x < kProfSlots) atomicAdd(&g_wgrad_prof[threadIdx.x], s_prof[threadIdx.x]);
+#endif
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
@@ -854,21 +964,36 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
 
 }  // namespace
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR = false>
 static cudaError_t launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                                const GemmParams& p, int grid, cudaStream_t stream) {
-  using C = Cfg<BN, EPI>;
+  using C = Cfg<BN, EPI, PAIR>;
   static int configured_device_mask = 0;  // bit per device ordinal (< 32)
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
   if (dev >= 32 || !(configured_device_mask & (1 << dev))) {
-    err = cudaFuncSetAttribute(grouped_wgrad_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    err = cudaFuncSetAttribute(grouped_wgrad_kernel<BN, EPI, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                C::SMEM_BYTES);
     if (err != cudaSuccess) return err;
     if (dev < 32) configured_device_mask |= (1 << dev);
   }
-  grouped_wgrad_kernel<BN, EPI><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tb, to, p);
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid & ~1));  // whole clusters of two
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, grouped_wgrad_kernel<BN, EPI, PAIR>, ta, tb, to, p);
+  }
+  grouped_wgrad_kernel<BN, EPI, PAIR><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tb, to, p);
   return cudaGetLastError();
 }
 
@@ -891,6 +1016,11 @@ static cudaError_t launch_ue8m0(const CUtensorMap& ta, const CUtensorMap& tb, co
 cudaError_t launch_grouped_wgrad(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                                  const GemmParams& p, int grid, cudaStream_t stream) {
   if (p.ue8m0) return p.bn == BsCfg::BN ? launch_ue8m0(ta, tb, to, p, grid, stream) : cudaErrorInvalidValue;
+  if (p.bm == 256) {
+    if (p.bn != 256) return cudaErrorInvalidValue;
+    return p.epi_warps == 16 ? launch_impl<256, 16, true>(ta, tb, to, p, grid, stream)
+                             : launch_impl<256, 8, true>(ta, tb, to, p, grid, stream);
+  }
   if (p.bn == 256) {
     return p.epi_warps == 16 ? launch_impl<256, 16>(ta, tb, to, p, grid, stream)
                              : launch_impl<256, 8>(ta, tb, to, p, grid, stream);

@@ -25,6 +25,9 @@ enum ProfSlot : int {
   kProfKBlocks = 8,             // count: K blocks promoted (first promotion warp)
   kProfTiles = 9,               // count: output tiles stored
   kProfCtas = 10,               // count: CTAs
+  kProfSfConvert = 11,          // UE8M0 scale-factor writer: scale loads, E8M0 conversion, shared stores
+  kProfSfPublish = 12,          // UE8M0 scale-factor writer: proxy fence and barrier arrivals
+  kProfLoadLatency = 13,        // operand stage: producer issue -> MMA warp sees it full
   kProfSlots = 16,
 };
 
@@ -52,7 +55,8 @@ struct GemmParams {
   const int32_t* expert_order;  // [E] or nullptr
   int num_experts;
   int m, n;
-  int bn;                       // tile N (128 or 256); tile M is 128
+  int bn;                       // tile N (128, 192 or 256)
+  int bm;                       // tile M: 128, or 256 for a CTA pair (cta_group::2)
   int tiles_n;
   int tiles_per_expert;
   int num_tiles;

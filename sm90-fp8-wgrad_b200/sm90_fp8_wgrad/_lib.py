@@ -35,6 +35,8 @@ TILE_128x256_W16 = 4
 TILE_128x128_2CTA = 5
 TILE_128x192_W12 = 6
 TILE_128x192_UE8M0 = 7
+TILE_256x256_PAIR = 8
+TILE_256x256_PAIR_W16 = 9
 SCALE_FP32 = 0
 SCALE_UE8M0 = 1
 
@@ -181,7 +183,8 @@ def check(status: int, what: str) -> None:
 
 
 PROFILE_SLOTS = ("producer_wait_stage", "producer_wait_scales", "mma_wait", "mma_issue", "epi_wait",
-                 "epi_promote", "epi_store", "epi_store_wait", "k_blocks", "tiles", "ctas")
+                 "epi_promote", "epi_store", "epi_store_wait", "k_blocks", "tiles", "ctas", "sf_convert",
+                 "sf_publish", "load_latency")
 
 
 def profile_counters() -> dict[str, int] | None:

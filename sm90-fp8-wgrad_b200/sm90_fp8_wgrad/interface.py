@@ -64,6 +64,8 @@ TUNED_CONFIGS: dict[str, int] = {
     "sm100_128x128_2cta": _lib.TILE_128x128_2CTA,  # two 128x128 pipelines (CTAs) per SM
     "sm100_128x192_w12": _lib.TILE_128x192_W12,    # 192-column tile, 12 promotion warps
     "sm100_128x192_ue8m0": _lib.TILE_128x192_UE8M0,  # power-of-two scales as tensor-core block scales
+    "sm100_256x256_pair": _lib.TILE_256x256_PAIR,    # CTA pair (cta_group::2), half of B per SM
+    "sm100_256x256_pair_w16": _lib.TILE_256x256_PAIR_W16,  # the same, 16 promotion warps per CTA
 }
 
 

@@ -28,6 +28,7 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="dsv3_32k")
     ap.add_argument("--tuned-config", default="default")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--scale-format", choices=("fp32", "ue8m0"), default="fp32")
     a = ap.parse_args(argv)
 
     import torch
@@ -43,7 +44,7 @@ def main(argv: list[str] | None = None) -> int:
     routing = make_routing(tokens=t, experts=e, top_k=k, route=route, seed=a.seed)
     inp = make_synthetic_wgrad_inputs(tokens=t, experts=e, top_k=k, hidden=h, intermediate=i, route=route,
                                       seed=a.seed, device=torch.device("cuda", torch.cuda.current_device()),
-                                      routing=routing)
+                                      routing=routing, scale_format=a.scale_format)
     inp.drop_sources()
     for name, fn in (("down", run_custom_down), ("gate_up", run_custom_gate_up)):
         fn(inp, tuned_config=a.tuned_config)
@@ -53,7 +54,10 @@ def main(argv: list[str] | None = None) -> int:
         torch.cuda.synchronize()
         c = _lib.profile_counters()
         blocks = max(c["k_blocks"], 1)
-        per_block = {key: round(v / blocks) for key, v in c.items() if key not in ("k_blocks", "tiles", "ctas")}
+        per_block = {key: round(v / blocks) for key, v in c.items()
+                     if key not in ("k_blocks", "tiles", "ctas") and (v or not key.startswith("sf_"))}
+        # load_latency is summed by the MMA warp over every K block it waited for
+        per_block["load_latency"] = round(c.get("load_latency", 0) / max(c["k_blocks"], 1))
         print(json.dumps({"workload": a.workload, "gemm": name, "ctas": c["ctas"],
                           "k_blocks_per_cta": round(c["k_blocks"] / max(c["ctas"], 1)),
                           "tiles_per_cta": round(c["tiles"] / max(c["ctas"], 1)),

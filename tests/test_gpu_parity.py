@@ -138,7 +138,9 @@ def test_quantiser_fp32_input_and_odd_columns(cuda_device):
     np.testing.assert_array_equal(op.scales.cpu().numpy().view(np.uint32), ref.scales.view(np.uint32))
 
 
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x128", "sm100_128x256_w8", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_128x192_w12"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x128", "sm100_128x256_w8", "sm100_128x256_w16",
+                                          "sm100_128x128_2cta", "sm100_128x192_w12", "sm100_256x256_pair",
+                                          "sm100_256x256_pair_w16"])
 @pytest.mark.parametrize("case", sorted(SMALL_CASES) + ["c1"])
 def test_grouped_wgrad_matches_oracle(cuda_device, case, tuned_config):
     from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
@@ -159,7 +161,8 @@ def test_grouped_wgrad_matches_oracle(cuda_device, case, tuned_config):
     assert _lib.device_error() == 0
 
 
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w8", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_128x192_w12"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w8", "sm100_128x256_w16", "sm100_128x128_2cta",
+                                          "sm100_128x192_w12", "sm100_256x256_pair"])
 def test_grouped_wgrad_fp32_out_and_accumulate(cuda_device, tuned_config):
     from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
 
@@ -185,7 +188,8 @@ def test_grouped_wgrad_fp32_out_and_accumulate(cuda_device, tuned_config):
     np.testing.assert_allclose(got, expect, rtol=2 ** -7, atol=1e-5 * float(np.abs(expect).max()))
 
 
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_128x192_w12"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_128x192_w12",
+                                          "sm100_256x256_pair"])
 @pytest.mark.parametrize("hidden,inter", [(144, 80), (272, 48), (512, 128)])
 def test_grouped_wgrad_ragged_tiles(cuda_device, hidden, inter, tuned_config):
     """M, N not multiples of the 128 x 256 tile; empty experts; long K."""
@@ -296,7 +300,7 @@ def test_legacy_quantiser_entry_point(cuda_device):
 
 @pytest.mark.parametrize("counts", [[0, 0, 0, 0], [300], [(e * 7) % 4 for e in range(1024)]],
                          ids=["all_empty", "one_expert", "1024_tiny_experts"])
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_256x256_pair"])
 def test_grouped_wgrad_edge_expert_sets(cuda_device, counts, tuned_config):
     """Every expert empty (no K rows at all: the launch has no operands and writes
     zeros), a single expert, and 1,024 experts of 0-3 rows each."""
