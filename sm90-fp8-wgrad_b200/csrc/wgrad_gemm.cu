@@ -704,16 +704,15 @@ struct BsCfg {
 };
 
 // E8M0 byte of a positive power-of-two fp32 scale, replicated into the four
-// bytes of a word. Anything else (mantissa bits, zero, subnormal, inf, NaN,
-// negative) sets device error 6 and encodes as 1.0.
-__device__ __forceinline__ uint32_t e8m0_word(float s) {
+// bytes of a word; anything else (mantissa bits, zero, subnormal, inf, NaN,
+// negative) encodes as 1.0 and sets `bad` (the caller records device error 6).
+// Branch-free, so a warp's scale loads can all be in flight together.
+__device__ __forceinline__ uint32_t e8m0_word(float s, bool& bad) {
   const uint32_t bits = __float_as_uint(s);
   const uint32_t e = bits >> 23;  // sign bit set -> e > 255
-  if ((bits & 0x7FFFFFu) != 0u || e == 0u || e >= 255u) {
-    record_device_error(kDevScaleNotPow2);
-    return 127u * 0x01010101u;
-  }
-  return e * 0x01010101u;
+  const bool invalid = (bits & 0x7FFFFFu) != 0u || e == 0u || e >= 255u;
+  bad |= invalid;
+  return (invalid ? 127u : e) * 0x01010101u;
 }
 
 __global__ void __launch_bounds__(BsCfg::THREADS, 1)
@@ -864,18 +863,32 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
         WGRAD_PROF_T(tf1);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
+        WGRAD_PROF_ADD(kProfSfSync, tf1);
+        WGRAD_PROF_T(tf3);
         const float* sc = s_scale + sstage * C::SCALE_FLOATS;
-        uint32_t w[12];  // A rows lane + 32 c (c < 4), then B rows lane + 32 (c - 4)
+        // A rows lane + 32 c (c < 4), then B rows lane + 32 (c - 4); rows past the
+        // operand's edge read as 1.0. All twelve loads first, then the conversion.
+        float v[12];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int r = lane + 32 * c;
-          w[c] = r < a_valid ? e8m0_word(sc[r]) : 127u * 0x01010101u;
+          v[c] = r < a_valid ? sc[r] : 1.0f;
         }
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const int r = lane + 32 * c;
-          w[4 + c] = (r < BN && r < b_valid) ? e8m0_word(sc[BM + r]) : 127u * 0x01010101u;
+          v[4 + c] = (r < BN && r < b_valid) ? sc[BM + r] : 1.0f;
         }
+        uint32_t w[12];
+        bool bad = false;
+#pragma unroll
+        for (int c = 0; c < 12; ++c) w[c] = e8m0_word(v[c], bad);
+        if (bad) record_device_error(kDevScaleNotPow2);
+#if WGRAD_PROFILE
+#pragma unroll
+        for (int i = 0; i < 12; ++i) asm volatile("" ::"r"(w[i]));  // the loads have landed
+        WGRAD_PROF_ADD(kProfSfLoad, tf3);
+#endif
         const uint32_t dst = smem_u32(s_sf + sfs * C::SF_STAGE_BYTES) + lane * 16;
         st_shared_v4(dst, w[0], w[1], w[2], w[3]);
         st_shared_v4(dst + C::SF_A_BYTES, w[4], w[5], w[6], w[7]);

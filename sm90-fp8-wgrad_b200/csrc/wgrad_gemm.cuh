@@ -28,6 +28,8 @@ enum ProfSlot : int {
   kProfSfConvert = 11,          // UE8M0 scale-factor writer: scale loads, E8M0 conversion, shared stores
   kProfSfPublish = 12,          // UE8M0 scale-factor writer: proxy fence and barrier arrivals
   kProfLoadLatency = 13,        // operand stage: producer issue -> MMA warp sees it full
+  kProfSfSync = 14,             // UE8M0 scale-factor writer: warp vote after its barrier wait
+  kProfSfLoad = 15,             // UE8M0 scale-factor writer: scale loads and E8M0 conversion
   kProfSlots = 16,
 };
 
