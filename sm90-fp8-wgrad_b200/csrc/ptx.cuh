@@ -311,7 +311,11 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// No memory clobber on the TMEM load path: volatile asm keeps these in order
+// with the barrier waits and tcgen05 fences around them, and the register
+// binding below orders the uses of the loaded values, so ordinary loads (the
+// scale vectors) stay free to be scheduled across them.
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;"); }
 
 // tcgen05.wait::ld, then re-define the destination registers of the loads it
 // waited for, so the compiler cannot schedule any use of them above the wait.
@@ -334,8 +338,7 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
         "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
         "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
+      : "r"(taddr));
 }
 
 // 32 lanes x 16 consecutive 32-bit columns.
@@ -345,8 +348,7 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
       "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
+      : "r"(taddr));
 }
 
 // Shared memory -> TMEM copy of a 32-row x 128-bit matrix, replicated into all

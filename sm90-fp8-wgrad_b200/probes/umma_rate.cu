@@ -178,6 +178,62 @@ int run(const char* name, int sms, int ring_kb, const uint8_t* src, unsigned lon
   return 0;
 }
 
+// TMEM read throughput: each of 4 * W warps (W per lane quarter) loads
+// 32 lanes x 32 columns (4 KB) per tcgen05.ld, `inflight` loads before each
+// wait, `reps` times; prints bytes per SM cycle.
+template <int INFLIGHT>
+__global__ void __launch_bounds__(512, 1) tmem_ld_rate_kernel(int reps, unsigned long long* out) {
+  __shared__ uint32_t holder;
+  const int warp = threadIdx.x >> 5;
+  if (warp == 0) {
+    tmem_alloc(&holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = holder + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+  const uint32_t col0 = static_cast<uint32_t>((warp >> 2) * 32 * INFLIGHT) & 511u;
+  uint32_t acc = 0;
+  const long long t0 = clock64();
+  for (int r = 0; r < reps; ++r) {
+    uint32_t v[INFLIGHT][32];
+#pragma unroll
+    for (int i = 0; i < INFLIGHT; ++i) tmem_ld_32x32b_x32(tmem + ((col0 + 32u * i) & 511u), v[i]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < INFLIGHT; ++i) acc ^= v[i][0] ^ v[i][31];
+  }
+  const long long t1 = clock64();
+  __syncthreads();
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    out[0] = static_cast<unsigned long long>(t1 - t0);
+    out[1] = acc;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(holder, 512);
+  }
+}
+
+template <int INFLIGHT>
+int run_tmem(int sms, int warps, unsigned long long* d_out) {
+  const int reps = 4096;
+  cudaMemset(d_out, 0, 2 * sizeof(unsigned long long));
+  tmem_ld_rate_kernel<INFLIGHT><<<sms, 32 * warps>>>(reps, d_out);
+  const cudaError_t err = cudaDeviceSynchronize();
+  unsigned long long h[2] = {0, 0};
+  cudaMemcpy(h, d_out, sizeof(h), cudaMemcpyDeviceToHost);
+  const double bytes = 4096.0 * INFLIGHT * reps * warps;  // per SM
+  std::printf("tcgen05.ld 32x32b.x32, %2d warps, %d in flight: %6.1f B/cycle/SM (%.1f cycles per 4 KB load), %s\n",
+              warps, INFLIGHT, h[0] ? bytes / static_cast<double>(h[0]) : 0.0,
+              h[0] ? static_cast<double>(h[0]) * warps / (static_cast<double>(reps) * INFLIGHT * warps) : 0.0,
+              cudaGetErrorString(err));
+  return err == cudaSuccess ? 0 : 1;
+}
+
 }  // namespace
 
 int main() {
@@ -198,6 +254,11 @@ int main() {
   rc |= run<128, false>("f8f6f4 N=128", sms, 0, src, d_out);
   rc |= run<192, true>("mxf8f6f4 N=192", sms, 0, src, d_out);
   rc |= run<192, true>("mxf8f6f4 N=192", sms, 64, src, d_out);
+  rc |= run_tmem<1>(sms, 4, d_out);
+  rc |= run_tmem<2>(sms, 4, d_out);
+  rc |= run_tmem<1>(sms, 8, d_out);
+  rc |= run_tmem<2>(sms, 8, d_out);
+  rc |= run_tmem<2>(sms, 16, d_out);
   cudaFree(src);
   cudaFree(d_out);
   return rc;
