@@ -214,15 +214,21 @@ SM100_WGRAD_API int sm100_wgrad_build_meta(const int32_t* cu_seqlens_k, int64_t 
  * diagnostics only, never call it inside a timed region). Writes one of the
  * device error codes to *code: 0 none; 1, 2, 3 a bounded wait of the GEMM's
  * producer, MMA or epilogue role expired; 4 bad tile; 5 a quantiser gather
- * index outside [0, x_rows). The first error since the last read is kept. */
+ * index outside [0, x_rows); 6 a scale given to the UE8M0 kernel that is not a
+ * positive power of two. The first error since the last read is kept. */
 SM100_WGRAD_API int sm100_wgrad_device_error(int32_t* code);
 
 /* Per-role cycle counters of the grouped GEMM, summed over CTAs since the last
  * read (synchronous; reads and clears). Only a library built with
  * -DWGRAD_PROFILE=1 (build_ext.py --profile) records them; the product build
- * returns SM100_WGRAD_ERR_UNSUPPORTED. Slots 0-10: producer wait for a stage,
- * producer wait for a scale stage, MMA wait, MMA issue, promotion wait,
- * promotion, tile store, wait for the previous store, K blocks, tiles, CTAs. */
+ * returns SM100_WGRAD_ERR_UNSUPPORTED. 24 slots. 0-10: producer wait for a
+ * stage, producer wait for a scale stage, MMA wait, MMA issue, promotion wait,
+ * promotion, tile store, wait for the previous store, K blocks, tiles, CTAs;
+ * 11-12: UE8M0 scale-factor writer conversion and publication; 13: operand
+ * stage latency (TMA issue to the MMA warp seeing the stage full); 14-15: UE8M0
+ * writer vote and scale loads; 16: UE8M0 MMA wait for a free accumulator. The
+ * UE8M0 kernel records its scale-factor writer in slots 4-5 and its epilogue's
+ * accumulator wait in slot 7. */
 SM100_WGRAD_API int sm100_wgrad_profile_counters(uint64_t* counters, int32_t n);
 
 /* Human-readable text of a status code (static storage). */

@@ -803,7 +803,9 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
       if (nkb == 0) continue;  // empty expert: the epilogue writes zeros without the accumulator
       const int klen = __ldg(p.k_row_offsets + tc.e + 1) - __ldg(p.k_row_offsets + tc.e);
       const int last_atoms = min(4, max(1, (klen - (nkb - 1) * BK + 31) / 32));
+      WGRAD_PROF_T(tt0);
       ok = mbar_wait(&tempty_bar[acc], aphase ^ 1u, abort_flag, kDevTimeoutMma);
+      WGRAD_PROF_ADD(kProfMmaTileWait, tt0);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();

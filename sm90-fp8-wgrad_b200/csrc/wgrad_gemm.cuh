@@ -30,7 +30,8 @@ enum ProfSlot : int {
   kProfLoadLatency = 13,        // operand stage: producer issue -> MMA warp sees it full
   kProfSfSync = 14,             // UE8M0 scale-factor writer: warp vote after its barrier wait
   kProfSfLoad = 15,             // UE8M0 scale-factor writer: scale loads and E8M0 conversion
-  kProfSlots = 16,
+  kProfMmaTileWait = 16,        // UE8M0 MMA warp: wait for a free accumulator at a tile's start
+  kProfSlots = 24,
 };
 
 #ifndef WGRAD_DEBUG_MODES

@@ -25,14 +25,14 @@ namespace {
 
 constexpr int kRing = 4;  // bulk-copy ring slots
 
-template <int N, bool MX>
+template <int N, bool MX, bool CP_EACH = false, bool RANDOM = false>
 __global__ void __launch_bounds__(128, 1)
     umma_rate_kernel(int iters, unsigned long long* out, const uint8_t* src, int ring_kb, int mma_on) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;                  // 128 rows x 128 B
   uint8_t* s_b = smem + 16384;          // N rows x 128 B
-  uint8_t* s_sf = s_b + N * 128;        // scale factors, 512 + 1024 B
+  uint8_t* s_sf = smem + (RANDOM ? 4 : 1) * (16384 + N * 128);  // scale factors, 512 + 1024 B
   uint8_t* ring = s_sf + 2048;          // bulk-copy ring
   __shared__ uint64_t done_bar, ring_bar[kRing];
   __shared__ uint32_t holder;
@@ -41,8 +41,20 @@ __global__ void __launch_bounds__(128, 1)
   __shared__ uint32_t chase[256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // e4m3 1.0 operands; E8M0 1.0 scale factors (127)
-  for (int i = threadIdx.x; i < (16384 + N * 128) / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(smem)[i] = 0x38383838u;
+  // e4m3 1.0 operands (RANDOM: four stages of pseudo-random finite e4m3 bytes,
+  // rotated per K block as the kernels' operand ring); E8M0 1.0 scale factors
+  constexpr int STAGE_BYTES = 16384 + N * 128;
+  for (int i = threadIdx.x; i < (RANDOM ? 4 : 1) * STAGE_BYTES / 4; i += blockDim.x) {
+    uint32_t w = 0x38383838u;
+    if (RANDOM) {
+      uint32_t h = static_cast<uint32_t>(i) * 2654435761u + blockIdx.x * 40503u;
+      h ^= h >> 13;
+      h *= 0x5bd1e995u;
+      h ^= h >> 15;
+      w = h & 0x77777777u;  // clear bit 7 and bit 3 of each byte: finite, |x| < 448
+    }
+    reinterpret_cast<uint32_t*>(smem)[i] = w;
+  }
   for (int i = threadIdx.x; i < 2048 / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(s_sf)[i] = 0x7F7F7F7Fu;
   if (threadIdx.x == 0) {
     mbar_init(&done_bar, 1);
@@ -74,10 +86,20 @@ __global__ void __launch_bounds__(128, 1)
     }
     const long long t0 = clock64();
     for (int it = 0; it < iters * mma_on; ++it) {
+      // CP_EACH: fresh scale factors for every K block, into one of 4 rotating
+      // 16-column TMEM stages, as the UE8M0 kernel copies them
+      const uint32_t sfs = CP_EACH ? sf + static_cast<uint32_t>((it & 3) * 16) : sf;
+      if (CP_EACH) {
+        tmem_cp_32x128b_warpx4(sfs, smem_desc_rows16(smem_u32(s_sf)));
+        tmem_cp_32x128b_warpx4(sfs + 4, smem_desc_rows16(smem_u32(s_sf) + 512));
+        tmem_cp_32x128b_warpx4(sfs + 8, smem_desc_rows16(smem_u32(s_sf) + 1024));
+      }
+      const uint32_t st = RANDOM ? static_cast<uint32_t>((it & 3) * (16384 + N * 128)) : 0u;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        if (MX) umma_mxf8(tmem, umma_desc_k_sw128(a + k * 32), umma_desc_k_sw128(b + k * 32), idesc, sf, sf + 4, 1u);
-        else umma_f8(tmem, umma_desc_k_sw128(a + k * 32), umma_desc_k_sw128(b + k * 32), idesc, 1u);
+        const uint64_t da = umma_desc_k_sw128(a + st + k * 32), db = umma_desc_k_sw128(b + st + k * 32);
+        if (MX) umma_mxf8(tmem, da, db, idesc, sfs, sfs + 4, 1u);
+        else umma_f8(tmem, da, db, idesc, 1u);
       }
     }
     umma_commit(&done_bar);
@@ -145,11 +167,11 @@ __global__ void __launch_bounds__(128, 1)
   }
 }
 
-template <int N, bool MX>
+template <int N, bool MX, bool CP_EACH = false, bool RANDOM = false>
 int run(const char* name, int sms, int ring_kb, const uint8_t* src, unsigned long long* d_out, int mma_on = 1) {
   const int iters = 4096;
-  const int smem = 1024 + 16384 + N * 128 + 2048 + ring_kb * 1024;
-  if (cudaFuncSetAttribute(umma_rate_kernel<N, MX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+  const int smem = 1024 + (RANDOM ? 4 : 1) * (16384 + N * 128) + 2048 + ring_kb * 1024;
+  if (cudaFuncSetAttribute(umma_rate_kernel<N, MX, CP_EACH, RANDOM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return 1;
   for (int rep = 0; rep < 2; ++rep) {
     cudaMemset(d_out, 0, 8 * sizeof(unsigned long long));
@@ -157,7 +179,7 @@ int run(const char* name, int sms, int ring_kb, const uint8_t* src, unsigned lon
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
     cudaEventRecord(e0);
-    umma_rate_kernel<N, MX><<<sms, 128, smem>>>(iters, d_out, src, ring_kb, mma_on);
+    umma_rate_kernel<N, MX, CP_EACH, RANDOM><<<sms, 128, smem>>>(iters, d_out, src, ring_kb, mma_on);
     cudaEventRecord(e1);
     const cudaError_t err = cudaEventSynchronize(e1);
     float ms = 0.f;
@@ -254,6 +276,9 @@ int main() {
   rc |= run<128, false>("f8f6f4 N=128", sms, 0, src, d_out);
   rc |= run<192, true>("mxf8f6f4 N=192", sms, 0, src, d_out);
   rc |= run<192, true>("mxf8f6f4 N=192", sms, 64, src, d_out);
+  rc |= run<192, true, true>("mxf8 N=192 +cp/blk", sms, 0, src, d_out);
+  rc |= run<192, true, true, true>("mxf8 N=192 rand4", sms, 0, src, d_out);
+  rc |= run<256, false, false, true>("f8f6f4 N=256 rand4", sms, 0, src, d_out);
   rc |= run_tmem<1>(sms, 4, d_out);
   rc |= run_tmem<2>(sms, 4, d_out);
   rc |= run_tmem<1>(sms, 8, d_out);

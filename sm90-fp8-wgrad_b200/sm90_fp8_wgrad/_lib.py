@@ -184,15 +184,15 @@ def check(status: int, what: str) -> None:
 
 PROFILE_SLOTS = ("producer_wait_stage", "producer_wait_scales", "mma_wait", "mma_issue", "epi_wait",
                  "epi_promote", "epi_store", "epi_store_wait", "k_blocks", "tiles", "ctas", "sf_convert",
-                 "sf_publish", "load_latency", "sf_sync", "sf_load")
+                 "sf_publish", "load_latency", "sf_sync", "sf_load", "mma_tile_wait")
 
 
 def profile_counters() -> dict[str, int] | None:
     """Per-role cycle counters of the grouped GEMM since the last call (read and
     cleared), or None when the loaded library was built without WGRAD_PROFILE
     (build one with ``build_ext.py --profile`` and point SM100_WGRAD_LIB at it)."""
-    buf = (ctypes.c_uint64 * 16)()
-    status = load().sm100_wgrad_profile_counters(buf, 16)
+    buf = (ctypes.c_uint64 * 24)()
+    status = load().sm100_wgrad_profile_counters(buf, 24)
     if int(status) == ERR_UNSUPPORTED:
         return None
     check(status, "sm100_wgrad_profile_counters")

@@ -55,7 +55,7 @@ def main(argv: list[str] | None = None) -> int:
         c = _lib.profile_counters()
         blocks = max(c["k_blocks"], 1)
         per_block = {key: round(v / blocks) for key, v in c.items()
-                     if key not in ("k_blocks", "tiles", "ctas") and (v or not key.startswith("sf_"))}
+                     if key not in ("k_blocks", "tiles", "ctas") and (v or not key.startswith(("sf_", "mma_tile")))}
         # load_latency is summed by the MMA warp over every K block it waited for
         per_block["load_latency"] = round(c.get("load_latency", 0) / max(c["k_blocks"], 1))
         print(json.dumps({"workload": a.workload, "gemm": name, "ctas": c["ctas"],
