@@ -67,14 +67,23 @@ extern "C" {
 /* 128x192 tile for UE8M0 scales: every scale must be a positive power of two
  * (the quantiser's scale_format 1); the tensor core applies them as E8M0 block
  * scales (tcgen05.mma kind::mxf8f6f4.block_scale) and no fp32 promotion runs.
- * A scale with mantissa bits set is taken as 1.0 and sets device error 6.
- * Never chosen by AUTO. */
+ * A scale with mantissa bits set is taken as 1.0 and sets device error 6
+ * (reported by sm100_wgrad_poll_device_error / sm100_wgrad_device_error).
+ * Never chosen by the C ABI's AUTO; the Python operator selects it for AUTO
+ * when both operands carry scale_format == "ue8m0". */
 #define SM100_WGRAD_TILE_128x192_UE8M0 7
 /* 256x256 tile over a pair of CTAs (a cluster of two on neighbouring SMs):
  * tcgen05.mma cta_group::2 with each CTA loading its 128 rows of lhs and half
  * of the rhs tile, 8 promotion warps per CTA. */
 #define SM100_WGRAD_TILE_256x256_PAIR 8
 #define SM100_WGRAD_TILE_256x256_PAIR_W16 9   /* the same with 16 promotion warps per CTA */
+/* 256x256 tile over a CTA pair whose per-block scale product lhs_s (x) rhs_s
+ * is computed by a TF32 UMMA on hi/lo splits of the scales, so the fp32
+ * promotion is one fused multiply-add per element. Needs a device workspace
+ * of sm100_wgrad_workspace_bytes() bytes (256-byte aligned) for the split
+ * scales, written by the call itself. */
+#define SM100_WGRAD_TILE_256x256_SP 10
+#define SM100_WGRAD_TILE_256x256_SP_W16 11   /* the same with 16 promotion warps per CTA */
 
 typedef struct Sm100WgradArgs {
   const void* lhs_data;      /* FP8 e4m3 [M][lhs_pitch]                              */
@@ -96,6 +105,9 @@ typedef struct Sm100WgradArgs {
   const int32_t* expert_order;   /* device [E] schedule order (LPT), or NULL = 0..E-1 */
   int32_t tile_config;       /* SM100_WGRAD_TILE_*                                   */
   int32_t max_ctas;          /* persistent grid cap, 0 = one CTA per SM              */
+  void* workspace;           /* device scratch, 256-byte aligned (see
+                                sm100_wgrad_workspace_bytes); NULL when it needs 0   */
+  int64_t workspace_bytes;   /* size of workspace                                    */
 } Sm100WgradArgs;
 
 /*
@@ -110,12 +122,21 @@ typedef struct Sm100WgradArgs {
  * scale block multiplies only its ceil(rows / 32) valid 32-row K slices.
  * A launch over an expert sub-range [e0, e1) passes num_experts = e1 - e0 and
  * block_offsets / k_row_offsets / out offset by e0 (their values stay absolute).
- * Environment read per launch: KERNEL_LAB_WGRAD_KERNEL_MODE (the reference's
- * known-answer modes coord_m / coord_n / scale_only / unscaled; only a library
- * built with -DWGRAD_DEBUG_MODES=1 runs them, others return
- * SM100_WGRAD_ERR_UNSUPPORTED) and SM100_WGRAD_DEBUG_INJECT (test-only).
+ * The product library reads no environment variable. A library built with
+ * -DWGRAD_DEBUG_MODES=1 (sm100_wgrad_build_flags) reads, per launch,
+ * KERNEL_LAB_WGRAD_KERNEL_MODE (the reference's known-answer modes coord_m /
+ * coord_n / scale_only / unscaled) and SM100_WGRAD_DEBUG_INJECT (test-only).
  */
 SM100_WGRAD_API int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* args, void* stream);
+
+/*
+ * Device workspace (bytes) that sm100_fp8_grouped_wgrad needs for these
+ * arguments: total_blocks * (m + n) * 16 (+ alignment) for
+ * SM100_WGRAD_TILE_256x256_SP(_W16), 0 for every other tile configuration. The
+ * reference allocates its scratch inside the launcher (gemm_sm90.py:5526-5899,
+ * through the framework's allocator); here the caller owns it.
+ */
+SM100_WGRAD_API int sm100_wgrad_workspace_bytes(const Sm100WgradArgs* args, int64_t* bytes);
 
 /*
  * 1x128 FP8 quantiser: per (128-row block b, column c)
@@ -217,6 +238,24 @@ SM100_WGRAD_API int sm100_wgrad_build_meta(const int32_t* cu_seqlens_k, int64_t 
  * index outside [0, x_rows); 6 a scale given to the UE8M0 kernel that is not a
  * positive power of two. The first error since the last read is kept. */
 SM100_WGRAD_API int sm100_wgrad_device_error(int32_t* code);
+
+/* Non-blocking form of sm100_wgrad_device_error: reads (and clears) a pinned,
+ * host-mapped copy of the device error word that every failing kernel writes
+ * with a system-scope fence, so a caller learns of a device-side failure of an
+ * earlier launch (a bounded wait that gave up, a bad gather index, a non-UE8M0
+ * scale) without synchronising the stream: *code is 0 when no launch that has
+ * finished so far recorded an error since the last poll or read. The reference
+ * has no device error channel (its failures surface as exceptions of the
+ * framework). The mirror is set up by the first call of any entry point on a
+ * device (a synchronous symbol copy: make that first call outside any CUDA
+ * stream capture); returns SM100_WGRAD_ERR_UNSUPPORTED if pinned mapped memory
+ * was unavailable. */
+SM100_WGRAD_API int sm100_wgrad_poll_device_error(int32_t* code);
+
+/* Compile-time features of the loaded library (bit mask). */
+#define SM100_WGRAD_BUILD_DEBUG_MODES 1 /* known-answer modes + test-only failure injection */
+#define SM100_WGRAD_BUILD_PROFILE 2     /* per-role cycle counters                          */
+SM100_WGRAD_API int sm100_wgrad_build_flags(void);
 
 /* Per-role cycle counters of the grouped GEMM, summed over CTAs since the last
  * read (synchronous; reads and clears). Only a library built with

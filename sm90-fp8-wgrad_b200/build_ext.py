@@ -6,9 +6,7 @@ Output: sm90-fp8-wgrad_b200/sm90_fp8_wgrad/_lib/libsm100_fp8_wgrad.so
         counters, -DWGRAD_PROFILE=1, read with sm90_fp8_wgrad._lib.profile_counters();
         --debug-modes: libsm100_fp8_wgrad_debug.so with the known-answer kernel
         modes of KERNEL_LAB_WGRAD_KERNEL_MODE, -DWGRAD_DEBUG_MODES=1. Load either
-        with SM100_WGRAD_LIB=<path>.
-        --probes: the stand-alone measurement programs under probes/, e.g.
-        sm90_fp8_wgrad/_lib/umma_rate, the UMMA issue-rate probe.)
+        with SM100_WGRAD_LIB=<path>.)
 """
 from __future__ import annotations
 
@@ -24,7 +22,6 @@ CSRC = HERE / "csrc"
 OUT = HERE / "sm90_fp8_wgrad" / "_lib" / "libsm100_fp8_wgrad.so"
 OUT_PROFILE = HERE / "sm90_fp8_wgrad" / "_lib" / "libsm100_fp8_wgrad_profile.so"
 OUT_DEBUG = HERE / "sm90_fp8_wgrad" / "_lib" / "libsm100_fp8_wgrad_debug.so"
-PROBES = HERE / "probes"
 SOURCES = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [HERE.parent / "include" / "sm100_fp8_wgrad.h"]
 
 
@@ -64,33 +61,11 @@ def build(force: bool = False, verbose: bool = False, profile: bool = False, deb
     return out
 
 
-def build_probes(force: bool = False) -> list[Path]:
-    """Compile each probes/*.cu into an executable beside the library."""
-    outs = []
-    for src in sorted(PROBES.glob("*.cu")):
-        out = OUT.parent / src.stem
-        deps = [src, CSRC / "ptx.cuh"]
-        if force or not out.exists() or any(d.stat().st_mtime > out.stat().st_mtime for d in deps):
-            out.parent.mkdir(parents=True, exist_ok=True)
-            cmd = [nvcc_path(), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
-                   "-o", str(out), str(src), "-lcuda"]
-            res = subprocess.run(cmd, capture_output=True, text=True)
-            if res.returncode != 0:
-                raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
-        outs.append(out)
-    return outs
-
-
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--profile", action="store_true", help="build the per-role cycle-counter library")
     ap.add_argument("--debug-modes", action="store_true", help="build the known-answer kernel-mode library")
-    ap.add_argument("--probes", action="store_true", help="build the measurement programs under probes/")
     a = ap.parse_args()
-    if a.probes:
-        for out in build_probes(force=a.force):
-            print(out)
-    else:
-        print(build(force=a.force, verbose=a.verbose, profile=a.profile, debug_modes=a.debug_modes))
+    print(build(force=a.force, verbose=a.verbose, profile=a.profile, debug_modes=a.debug_modes))

@@ -22,7 +22,17 @@ cudaError_t launch_quantize_1x128(const void* x, int x_dtype, int64_t cols, cons
                                   float* scales, int block_rows, int64_t x_rows, bool ue8m0, cudaStream_t stream);
 cudaError_t launch_build_meta(const int32_t* cu, int64_t num_experts, const Sm100WgradMetaOut& out,
                               cudaStream_t stream);
+cudaError_t launch_scale_operands(const float* sa, const float* sb, void* opa, void* opb, int64_t m, int64_t n,
+                                  const int32_t* block_offsets, int num_experts, int64_t total_blocks, int sm_count,
+                                  cudaStream_t stream);
+cudaError_t launch_grouped_wgrad_sp(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa,
+                                    const CUtensorMap& tsb, const CUtensorMap& to, const GemmParams& p, int grid,
+                                    cudaStream_t stream);
 }  // namespace wgrad
+
+#ifndef WGRAD_OPERAND_L2_PROMOTION
+#define WGRAD_OPERAND_L2_PROMOTION CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+#endif
 
 namespace {
 
@@ -41,6 +51,67 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     }
   });
   return fn;
+}
+
+// Tensor maps encoded for earlier launches, keyed by every argument of the
+// encoding (device, element type, rank, base address, extents, strides, box,
+// swizzle, L2 promotion). A map depends only on those values, never on the
+// memory's contents, so a hit is exact. A launch needs three to five maps;
+// the cache saves their encoding on repeated launches over the same buffers
+// (the reference caches its compiled launch per shape, gemm_sm90.py:5388-5409).
+struct MapKey {
+  int dev, dtype, rank, swizzle, promo;
+  const void* ptr;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3];
+  bool operator==(const MapKey& o) const {
+    return dev == o.dev && dtype == o.dtype && rank == o.rank && swizzle == o.swizzle && promo == o.promo &&
+           ptr == o.ptr && std::memcmp(dims, o.dims, sizeof(dims)) == 0 &&
+           std::memcmp(strides, o.strides, sizeof(strides)) == 0 && std::memcmp(box, o.box, sizeof(box)) == 0;
+  }
+};
+
+int cached_encode(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* ptr, const cuuint64_t* dims,
+                  const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swizzle,
+                  CUtensorMapL2promotion promo) {
+  constexpr int kSlots = 64;
+  static std::mutex mu;
+  static MapKey keys[kSlots];
+  static CUtensorMap maps[kSlots];
+  static int used = 0, next = 0;
+  MapKey k{};
+  if (cudaGetDevice(&k.dev) != cudaSuccess) return SM100_WGRAD_ERR_LAUNCH;
+  k.dtype = static_cast<int>(dtype);
+  k.rank = rank;
+  k.swizzle = static_cast<int>(swizzle);
+  k.promo = static_cast<int>(promo);
+  k.ptr = ptr;
+  for (int i = 0; i < rank; ++i) {
+    k.dims[i] = dims[i];
+    k.box[i] = box[i];
+    if (i + 1 < rank) k.strides[i] = strides[i];
+  }
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i) {
+      if (keys[i] == k) {
+        *map = maps[i];
+        return SM100_WGRAD_OK;
+      }
+    }
+  }
+  auto encode = get_encode_fn();
+  if (encode == nullptr) return SM100_WGRAD_ERR_LAUNCH;
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUresult r = encode(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(ptr), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return SM100_WGRAD_ERR_TENSOR_MAP;
+  std::lock_guard<std::mutex> lock(mu);
+  keys[next] = k;
+  maps[next] = *map;
+  next = (next + 1) % kSlots;
+  if (used < kSlots) ++used;
+  return SM100_WGRAD_OK;
 }
 
 // Per-device capability check and SM count, cached.
@@ -71,11 +142,42 @@ int device_info(DeviceInfo* info) {
   return SM100_WGRAD_OK;
 }
 
+// Per-device host-mapped mirror of the device error word: one pinned word,
+// mapped into the device's address space and published to the kernels'
+// g_device_error_host once (a synchronous symbol copy on the first call of
+// any entry point on that device, which must therefore not be inside a CUDA
+// stream capture). Null when pinned mapped memory is unavailable.
+volatile unsigned int* error_mirror(int dev) {
+  static std::once_flag flags[wgrad::kMaxDevices];
+  static volatile unsigned int* words[wgrad::kMaxDevices] = {};
+  if (dev < 0 || dev >= wgrad::kMaxDevices) return nullptr;
+  std::call_once(flags[dev], [dev] {
+    void* h = nullptr;
+    if (cudaHostAlloc(&h, sizeof(unsigned int), cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return;
+    }
+    *static_cast<volatile unsigned int*>(h) = 0u;
+    void* d = nullptr;
+    if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess ||
+        cudaMemcpyToSymbol(wgrad::g_device_error_host, &d, sizeof(d)) != cudaSuccess) {
+      (void)cudaGetLastError();
+      cudaFreeHost(h);
+      return;
+    }
+    words[dev] = static_cast<volatile unsigned int*>(h);
+  });
+  return words[dev];
+}
+
 int check_arch(DeviceInfo* info) {
   const int st = device_info(info);
   if (st != SM100_WGRAD_OK) return st;
   // sm_100a code runs on compute capability 10.0 only.
   if (info->major != 10 || info->minor != 0) return SM100_WGRAD_ERR_UNSUPPORTED_ARCH;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SM100_WGRAD_ERR_LAUNCH;
+  (void)error_mirror(dev);
   return SM100_WGRAD_OK;
 }
 
@@ -84,35 +186,48 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // FP8 operand [cols][pitch] bytes, box = 128 K-bytes x box_rows columns, 128B swizzle.
 int encode_operand_map(CUtensorMap* map, const void* data, int64_t k_rows, int64_t cols, int64_t pitch,
                        int box_rows) {
-  auto encode = get_encode_fn();
-  if (encode == nullptr) return SM100_WGRAD_ERR_LAUNCH;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k_rows), static_cast<cuuint64_t>(cols)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
   const cuuint32_t box[2] = {128u, static_cast<cuuint32_t>(box_rows)};
-  const cuuint32_t estr[2] = {1u, 1u};
-  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(data), dims, strides, box, estr,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? SM100_WGRAD_OK : SM100_WGRAD_ERR_TENSOR_MAP;
+  return cached_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, data, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                       WGRAD_OPERAND_L2_PROMOTION);
 }
 
-// Output [E][M][N]; box = (64 bf16 | 32 fp32) columns x 32 rows x 1 expert, 128B swizzle.
-int encode_out_map(CUtensorMap* map, void* out, int out_f32, int64_t e, int64_t m, int64_t n) {
-  auto encode = get_encode_fn();
-  if (encode == nullptr) return SM100_WGRAD_ERR_LAUNCH;
+// Output [E][M][N]; box = (64 bf16 | 32 fp32) columns x 32 rows x 1 expert,
+// 128B swizzle; narrow_bf16: 32-column bf16 boxes (64-byte rows, 64B swizzle).
+int encode_out_map(CUtensorMap* map, void* out, int out_f32, int64_t e, int64_t m, int64_t n,
+                   bool narrow_bf16 = false) {
   const int64_t esz = out_f32 ? 4 : 2;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m), static_cast<cuuint64_t>(e)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(n * esz), static_cast<cuuint64_t>(m * n * esz)};
-  const cuuint32_t box[3] = {out_f32 ? 32u : 64u, 32u, 1u};
-  const cuuint32_t estr[3] = {1u, 1u, 1u};
-  const CUresult r =
-      encode(map, out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dims, strides,
-             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? SM100_WGRAD_OK : SM100_WGRAD_ERR_TENSOR_MAP;
+  const bool narrow = narrow_bf16 && !out_f32;
+  const cuuint32_t box[3] = {out_f32 || narrow ? 32u : 64u, 32u, 1u};
+  return cached_encode(map, out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dims,
+                       strides, box, narrow ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                       CU_TENSOR_MAP_L2_PROMOTION_NONE);
+}
+
+// Split-scale operand of the scale-product kernel: [blocks][cols][4] fp32
+// (16 B per scale), read as boxes of 8 x box_rows x 1 with 32-byte swizzling;
+// the box's four K elements past the 16-byte row lie outside the tensor and
+// are zero-filled by the TMA unit.
+int encode_scale_operand_map(CUtensorMap* map, void* data, int64_t cols, int64_t blocks, int box_rows) {
+  const cuuint64_t dims[3] = {4u, static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(blocks)};
+  const cuuint64_t strides[2] = {16u, static_cast<cuuint64_t>(cols * 16)};
+  const cuuint32_t box[3] = {8u, static_cast<cuuint32_t>(box_rows), 1u};
+  return cached_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, data, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_32B,
+                       CU_TENSOR_MAP_L2_PROMOTION_NONE);
+}
+
+// Workspace of the scale-product kernel: the split lhs scales [blocks][m][4]
+// fp32, then (256-byte aligned) the split rhs scales [blocks][n][4].
+int64_t sp_workspace_lhs_bytes(int64_t blocks, int64_t m) { return (blocks * m * 16 + 255) / 256 * 256; }
+int64_t sp_workspace_bytes(int64_t blocks, int64_t m, int64_t n) {
+  return sp_workspace_lhs_bytes(blocks, m) + blocks * n * 16;
 }
 
 int pick_bn(int32_t tile_config, int64_t n) {
+  if (tile_config == SM100_WGRAD_TILE_256x256_SP || tile_config == SM100_WGRAD_TILE_256x256_SP_W16) return 256;
   if (tile_config == SM100_WGRAD_TILE_128x128 || tile_config == SM100_WGRAD_TILE_128x128_2CTA) return 128;
   if (tile_config == SM100_WGRAD_TILE_128x192_W12 || tile_config == SM100_WGRAD_TILE_128x192_UE8M0) return 192;
   if (tile_config == SM100_WGRAD_TILE_128x256 || tile_config == SM100_WGRAD_TILE_128x256_W8 ||
@@ -133,7 +248,10 @@ int pick_epi_warps(int32_t tile_config, int bn, int64_t total_blocks, int64_t nu
   if (tile_config == SM100_WGRAD_TILE_128x128_2CTA) return 4;
   if (tile_config == SM100_WGRAD_TILE_128x192_W12 || tile_config == SM100_WGRAD_TILE_128x192_UE8M0) return 12;
   if (bn != 256 || tile_config == SM100_WGRAD_TILE_128x256_W8 || tile_config == SM100_WGRAD_TILE_256x256_PAIR) return 8;
-  if (tile_config == SM100_WGRAD_TILE_128x256_W16 || tile_config == SM100_WGRAD_TILE_256x256_PAIR_W16) return 16;
+  if (tile_config == SM100_WGRAD_TILE_128x256_W16 || tile_config == SM100_WGRAD_TILE_256x256_PAIR_W16 ||
+      tile_config == SM100_WGRAD_TILE_256x256_SP_W16)
+    return 16;
+  if (tile_config == SM100_WGRAD_TILE_256x256_SP) return 8;
   return total_blocks <= kShortKBlocksPerExpert * num_experts ? 16 : 8;
 }
 
@@ -162,7 +280,7 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   if (a->num_experts < 0 || a->m <= 0 || a->n <= 0 || a->k_rows < 0 || a->total_blocks < 0)
     return SM100_WGRAD_ERR_INVALID_ARG;
   if (a->out_dtype != SM100_WGRAD_OUT_BF16 && a->out_dtype != SM100_WGRAD_OUT_F32) return SM100_WGRAD_ERR_INVALID_ARG;
-  if (a->tile_config < SM100_WGRAD_TILE_AUTO || a->tile_config > SM100_WGRAD_TILE_256x256_PAIR_W16)
+  if (a->tile_config < SM100_WGRAD_TILE_AUTO || a->tile_config > SM100_WGRAD_TILE_256x256_SP_W16)
     return SM100_WGRAD_ERR_INVALID_ARG;
   // TMA: output row pitch and scale-vector chunks must be 16-byte multiples.
   if (a->m % 16 != 0 || a->n % 16 != 0) return SM100_WGRAD_ERR_UNSUPPORTED;
@@ -185,18 +303,36 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   if (st != SM100_WGRAD_OK) return st;
 
   const int bn = pick_bn(a->tile_config, a->n);
-  const bool pair =
-      a->tile_config == SM100_WGRAD_TILE_256x256_PAIR || a->tile_config == SM100_WGRAD_TILE_256x256_PAIR_W16;
+  const bool sp = a->tile_config == SM100_WGRAD_TILE_256x256_SP || a->tile_config == SM100_WGRAD_TILE_256x256_SP_W16;
+  const bool pair = sp || a->tile_config == SM100_WGRAD_TILE_256x256_PAIR ||
+                    a->tile_config == SM100_WGRAD_TILE_256x256_PAIR_W16;
   const int bm = pair ? 256 : 128;
-  CUtensorMap ta{}, tb{}, to{};
+  CUtensorMap ta{}, tb{}, to{}, tsa{}, tsb{};
+  void* opa = nullptr;
+  void* opb = nullptr;
+  if (sp && has_operands) {
+    const int64_t need = sp_workspace_bytes(a->total_blocks, a->m, a->n);
+    if (a->workspace == nullptr || a->workspace_bytes < need || (reinterpret_cast<uintptr_t>(a->workspace) & 255u))
+      return SM100_WGRAD_ERR_INVALID_ARG;
+    opa = a->workspace;
+    opb = static_cast<uint8_t*>(a->workspace) + sp_workspace_lhs_bytes(a->total_blocks, a->m);
+  }
   if (has_operands) {
     st = encode_operand_map(&ta, a->lhs_data, a->k_rows, a->m, a->lhs_pitch, 128);
     if (st != SM100_WGRAD_OK) return st;
-    // a pair CTA loads half of the rhs tile's rows
-    st = encode_operand_map(&tb, a->rhs_data, a->k_rows, a->n, a->rhs_pitch, pair ? bn / 2 : bn);
+    // a pair CTA loads half of the rhs tile's rows (the scale-product kernel:
+    // half of each 128-column half)
+    st = encode_operand_map(&tb, a->rhs_data, a->k_rows, a->n, a->rhs_pitch, sp ? 64 : (pair ? bn / 2 : bn));
     if (st != SM100_WGRAD_OK) return st;
+    if (sp) {
+      st = encode_scale_operand_map(&tsa, opa, a->m, a->total_blocks, 128);
+      if (st != SM100_WGRAD_OK) return st;
+      st = encode_scale_operand_map(&tsb, opb, a->n, a->total_blocks, 64);
+      if (st != SM100_WGRAD_OK) return st;
+    }
   }
-  st = encode_out_map(&to, a->out, a->out_dtype == SM100_WGRAD_OUT_F32, a->num_experts, a->m, a->n);
+  st = encode_out_map(&to, a->out, a->out_dtype == SM100_WGRAD_OUT_F32, a->num_experts, a->m, a->n,
+                      a->tile_config == SM100_WGRAD_TILE_256x256_SP_W16);
   if (st != SM100_WGRAD_OK) return st;
 
   GemmParams p{};
@@ -222,9 +358,12 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   p.accumulate = a->accumulate != 0;
   p.has_operands = has_operands ? 1 : 0;
   p.epi_warps = pick_epi_warps(a->tile_config, bn, a->total_blocks, a->num_experts);
-  // Known-answer kernel modes (KERNEL_LAB_WGRAD_KERNEL_MODE, as the reference):
-  // honoured by instrumented builds only; the product build refuses them.
+  // Known-answer kernel modes (KERNEL_LAB_WGRAD_KERNEL_MODE, as the reference)
+  // and the test-only failure injection exist in the debug-modes library only;
+  // the product library reads no environment variable.
   p.mode = wgrad::kModeNormal;
+  p.inject = 0;
+#if WGRAD_DEBUG_MODES
   if (const char* km = std::getenv("KERNEL_LAB_WGRAD_KERNEL_MODE"); km != nullptr && km[0] != '\0' &&
       std::strcmp(km, "normal") != 0) {
     if (std::strcmp(km, "coord_m") == 0) p.mode = wgrad::kModeCoordM;
@@ -232,15 +371,16 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
     else if (std::strcmp(km, "scale_only") == 0) p.mode = wgrad::kModeScaleOnly;
     else if (std::strcmp(km, "unscaled") == 0) p.mode = wgrad::kModeUnscaled;
     else return SM100_WGRAD_ERR_INVALID_ARG;
-    if (!WGRAD_DEBUG_MODES) return SM100_WGRAD_ERR_UNSUPPORTED;
   }
+  // Test-only failure injection of the bounded-wait path.
+  if (const char* inject = std::getenv("SM100_WGRAD_DEBUG_INJECT");
+      inject != nullptr && std::strcmp(inject, "withhold_first_load") == 0)
+    p.inject = wgrad::kInjectWithholdFirstLoad;
+#endif
   p.ue8m0 = a->tile_config == SM100_WGRAD_TILE_128x192_UE8M0 ? 1 : 0;
   // The known-answer modes instrument the promotion loop, which the UE8M0 kernel does not have.
   if (p.ue8m0 && p.mode != wgrad::kModeNormal) return SM100_WGRAD_ERR_UNSUPPORTED;
-  if (pair && p.mode != wgrad::kModeNormal) return SM100_WGRAD_ERR_UNSUPPORTED;
-  // Test-only failure injection of the bounded-wait path (never set in normal use).
-  const char* inject = std::getenv("SM100_WGRAD_DEBUG_INJECT");
-  p.inject = (inject != nullptr && std::strcmp(inject, "withhold_first_load") == 0) ? wgrad::kInjectWithholdFirstLoad : 0;
+  if (pair && !sp && p.mode != wgrad::kModeNormal) return SM100_WGRAD_ERR_UNSUPPORTED;
 
   int grid = info.sm_count * (p.epi_warps == 4 ? 2 : 1);  // the 4-warp tile runs two CTAs per SM
   if (a->max_ctas > 0 && a->max_ctas < grid) grid = a->max_ctas;
@@ -252,8 +392,26 @@ int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* a, void* stream) {
   } else if (num_tiles < grid) {
     grid = static_cast<int>(num_tiles);
   }
+  if (sp) {
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (has_operands) {
+      cudaError_t e = wgrad::launch_scale_operands(a->lhs_scales, a->rhs_scales, opa, opb, a->m, a->n,
+                                                   a->block_offsets, p.num_experts, a->total_blocks, info.sm_count, s);
+      if (e != cudaSuccess) return SM100_WGRAD_ERR_LAUNCH;
+    }
+    const cudaError_t e = wgrad::launch_grouped_wgrad_sp(ta, tb, tsa, tsb, to, p, grid, s);
+    return e == cudaSuccess ? SM100_WGRAD_OK : SM100_WGRAD_ERR_LAUNCH;
+  }
   const cudaError_t err = wgrad::launch_grouped_wgrad(ta, tb, to, p, grid, static_cast<cudaStream_t>(stream));
   return err == cudaSuccess ? SM100_WGRAD_OK : SM100_WGRAD_ERR_LAUNCH;
+}
+
+int sm100_wgrad_workspace_bytes(const Sm100WgradArgs* a, int64_t* bytes) {
+  if (a == nullptr || bytes == nullptr) return SM100_WGRAD_ERR_INVALID_ARG;
+  if (a->m <= 0 || a->n <= 0 || a->total_blocks < 0) return SM100_WGRAD_ERR_INVALID_ARG;
+  const bool sp = a->tile_config == SM100_WGRAD_TILE_256x256_SP || a->tile_config == SM100_WGRAD_TILE_256x256_SP_W16;
+  *bytes = sp ? sp_workspace_bytes(a->total_blocks, a->m, a->n) : 0;
+  return SM100_WGRAD_OK;
 }
 
 int sm100_wgrad_quantize_1x128(const void* x, int32_t x_dtype, int64_t valid_rows, int64_t cols,
@@ -343,8 +501,29 @@ int sm100_wgrad_device_error(int32_t* code) {
   if (cudaMemcpyFromSymbol(&v, wgrad::g_device_error, sizeof(v)) != cudaSuccess) return SM100_WGRAD_ERR_LAUNCH;
   if (v != 0 && cudaMemcpyToSymbol(wgrad::g_device_error, &zero, sizeof(zero)) != cudaSuccess)
     return SM100_WGRAD_ERR_LAUNCH;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) {
+    if (volatile unsigned int* w = error_mirror(dev)) *w = 0u;  // reported here: nothing left pending
+  }
   *code = static_cast<int32_t>(v);
   return SM100_WGRAD_OK;
+}
+
+int sm100_wgrad_poll_device_error(int32_t* code) {
+  if (code == nullptr) return SM100_WGRAD_ERR_INVALID_ARG;
+  *code = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SM100_WGRAD_ERR_LAUNCH;
+  volatile unsigned int* w = error_mirror(dev);
+  if (w == nullptr) return SM100_WGRAD_ERR_UNSUPPORTED;
+  const unsigned int v = *w;
+  if (v != 0u) *w = 0u;
+  *code = static_cast<int32_t>(v);
+  return SM100_WGRAD_OK;
+}
+
+int sm100_wgrad_build_flags(void) {
+  return (WGRAD_DEBUG_MODES ? SM100_WGRAD_BUILD_DEBUG_MODES : 0) | (WGRAD_PROFILE ? SM100_WGRAD_BUILD_PROFILE : 0);
 }
 
 }  // extern "C"

@@ -30,6 +30,10 @@ enum DeviceError : unsigned int {
 
 // Module-global device error word (read and cleared by sm100_wgrad_device_error).
 __device__ unsigned int g_device_error = 0;
+// Host-mapped mirror of the error word (one pinned host word per device, set
+// once by the C ABI before the first launch on that device); the host polls
+// it without synchronising (sm100_wgrad_poll_device_error).
+__device__ unsigned int* g_device_error_host = nullptr;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -43,6 +47,11 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 __device__ __forceinline__ void record_device_error(unsigned int code) {
   atomicCAS(&g_device_error, 0u, code);
+  unsigned int* host = g_device_error_host;
+  if (host != nullptr) {
+    *reinterpret_cast<volatile unsigned int*>(host) = code;  // plain store: PCIe has no host-side atomics
+    __threadfence_system();
+  }
 }
 
 // ---------------------------------------------------------------- mbarrier
@@ -250,6 +259,26 @@ __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorM
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
       : "memory");
 }
+// Tiled 3-D load into this CTA's shared memory completing on an mbarrier of
+// either CTA of the pair (see tma_load_2d_pair).
+__device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster_addr,
+                                                 int32_t c0, int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+// Pair UMMA on 32-bit operands read as TF32 (kind::tf32), F32 accumulate.
+__device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void umma_f8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                              uint32_t accumulate) {
   asm volatile(
@@ -384,6 +413,27 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory matrix descriptor for a K-major operand tile written by TMA
+// with 32-byte swizzling: rows of 32 bytes (eight 32-bit K elements), 8-row
+// core groups 256 bytes apart, layout type 6 = SWIZZLE_32B.
+__device__ __forceinline__ uint64_t umma_desc_k_sw32(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;                 // LBO (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(256u >> 4) << 32;          // SBO: 8 rows x 32 B
+  d |= static_cast<uint64_t>(1u) << 46;                 // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(6u) << 61;                 // SWIZZLE_32B
+  return d;
+}
+
+// Instruction descriptor for kind::tf32: TF32 x TF32 -> F32, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_tf32_f32(int m, int n) {
+  return (1u << 4)                                  // D format F32
+         | (2u << 7) | (2u << 10)                   // A, B = TF32
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N >> 3
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M >> 4
+}
+
 // Instruction descriptor for kind::f8f6f4: E4M3 x E4M3 -> F32, both K-major.
 __host__ __device__ constexpr uint32_t umma_idesc_e4m3_f32(int m, int n) {
   return (1u << 4)                                  // D format F32
@@ -400,6 +450,13 @@ __host__ __device__ constexpr uint32_t umma_idesc_mxf8_e4m3_ue8m0(int m, int n) 
          | (static_cast<uint32_t>(n >> 3) << 17)    // N >> 3
          | (1u << 23)                               // scale format UE8M0
          | (static_cast<uint32_t>(m >> 4) << 24);   // M >> 4
+}
+
+// One elected lane of the (converged) warp returns true (elect.sync).
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t pred = 0;
+  asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}" : "=r"(pred));
+  return pred != 0;
 }
 
 // Warpgroup register re-allocation (all 128 threads of the warpgroup execute it).

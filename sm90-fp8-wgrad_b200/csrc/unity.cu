@@ -2,6 +2,7 @@
 // and the kernels that write it live in one module without relocatable
 // device code.
 #include "wgrad_gemm.cu"
+#include "wgrad_sp.cu"
 #include "quant.cu"
 #include "meta.cu"
 #include "capi.cu"

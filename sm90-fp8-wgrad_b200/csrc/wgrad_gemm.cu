@@ -40,6 +40,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "ptx.cuh"
 #include "wgrad_gemm.cuh"
@@ -83,6 +84,18 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 128;  // scale block == K block, bytes per row of an FP8 tile
 constexpr int SCALE_STAGES = 6;
+#ifndef WGRAD_PAIR_STAGES
+#define WGRAD_PAIR_STAGES 4
+#endif
+#ifndef WGRAD_PAIR_OUT_STAGE
+#define WGRAD_PAIR_OUT_STAGE 8192
+#endif
+#ifndef WGRAD_MMA_ELECT
+#define WGRAD_MMA_ELECT 1  // issue UMMAs from an elect.sync-chosen lane (measured faster than lane == 0)
+#endif
+#ifndef WGRAD_KROT
+#define WGRAD_KROT 0
+#endif
 constexpr int FIRST_EPI_WARP = 4;
 
 // Promotion warps: EPI = 4, 8 or 16 (one, two or four per TMEM lane quarter);
@@ -104,7 +117,7 @@ struct Cfg {
   static constexpr int THREADS = 32 * (4 + EPI_WARPS);
   static constexpr int CTAS_PER_SM = EPI_WARPS == 4 ? 2 : 1;
   // A pair CTA holds half of B, so a stage is 32 KB instead of 48 KB.
-  static constexpr int STAGES = PAIR ? 4 : (EPI_WARPS == 4 ? 2 : 3);
+  static constexpr int STAGES = PAIR ? WGRAD_PAIR_STAGES : (EPI_WARPS == 4 ? 2 : 3);
   static constexpr uint32_t REGS_CONTROL = EPI_WARPS == 16 ? 32 : (EPI_WARPS == 12 ? 40 : 56);
   static constexpr uint32_t REGS_EPILOGUE =
       EPI_WARPS == 16 ? 112 : (EPI_WARPS == 12 ? 152 : (EPI_WARPS == 4 ? 200 : 224));
@@ -116,7 +129,8 @@ struct Cfg {
   // tcgen05.ld columns per load: 32 when two such buffers fit beside the accumulator
   static constexpr int CHUNK = REGS_EPILOGUE >= COLS_PER_WARP + 80 ? 32 : 16;
   static constexpr int CHUNKS = COLS_PER_WARP / CHUNK;
-  static constexpr int OUT_STAGE_BYTES_PER_WARP = COLS_PER_WARP * 32 * 2 >= 8192 ? 8192 : 4096;
+  static constexpr int OUT_STAGE_BYTES_PER_WARP =
+      PAIR ? WGRAD_PAIR_OUT_STAGE : (COLS_PER_WARP * 32 * 2 >= 8192 ? 8192 : 4096);
   // double-buffered partial, allocated as a power of two (192-wide tiles use 384 of 512)
   static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
   static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + EPI_WARPS * OUT_STAGE_BYTES_PER_WARP +
@@ -200,7 +214,9 @@ __device__ __forceinline__ void run_producer(const CUtensorMap& tmap_a, const CU
     // the odd CTA of a pair may lie wholly below the last row of M
     const uint32_t a_scale_bytes = static_cast<uint32_t>(max(0, min(BM, p.m - tc.m0))) * 4u;
     const uint32_t b_scale_bytes = static_cast<uint32_t>(min(BN, p.n - tc.n0)) * 4u;
-    for (int kb = 0; kb < nkb && ok; ++kb) {
+    const int krot = (WGRAD_KROT && nkb > 1) ? (tc.e + tc.m0 / p.bm + tc.n0 / p.bn) % nkb : 0;
+    for (int kb_i = 0; kb_i < nkb && ok; ++kb_i) {
+      const int kb = kb_i + krot < nkb ? kb_i + krot : kb_i + krot - nkb;
       WGRAD_PROF_T(tw0);
       ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, kDevTimeoutProducer);
       WGRAD_PROF_ADD(kProfProducerWaitStage, tw0);
@@ -209,7 +225,7 @@ __device__ __forceinline__ void run_producer(const CUtensorMap& tmap_a, const CU
       // Test-only failure injection: announce the first stage's bytes but
       // issue no copy, so the stage never fills and the bounded waits of
       // the consumers expire (device error word, clean exit).
-      const bool withhold = p.inject == kInjectWithholdFirstLoad && tile == tile_begin && kb == 0;
+      const bool withhold = p.inject == kInjectWithholdFirstLoad && tile == tile_begin && kb_i == 0;
       if constexpr (PAIR) {
         const uint32_t leader_full = cluster_addr(&full_bar[stage], 0);
         if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * (C::A_BYTES + C::B_BYTES));
@@ -249,31 +265,38 @@ __device__ __forceinline__ void run_producer(const CUtensorMap& tmap_a, const CU
 }
 
 // Writes one warp's finished 32 rows x COLS columns (fin, fp32) of tile tc:
-// BF16 (or fp32) into the warp's 128B-swizzled staging area, then TMA stores
-// of 32-row boxes clipped to the output; with accumulate the previous output
-// boxes are first loaded through the same tensor map and added. The caller
-// has waited for the warp's previous store to finish reading the staging
-// area. Returns false when a wait gave up.
-template <int COLS, int OUT_STAGE_BYTES>
+// BF16 (or fp32) into the warp's swizzled staging area, then TMA stores of
+// 32-row boxes clipped to the output; with accumulate the previous output
+// boxes are first loaded through the same tensor map and added. fin holds
+// groups of GCOLS columns, GSTRIDE output columns apart (contiguous when
+// GSTRIDE == GCOLS). BF16 boxes are BOXC columns wide: 64 (128-byte rows,
+// 128B swizzle) or 32 (64-byte rows, 64B swizzle; the output tensor map must
+// match); fp32 boxes are 32 columns (128B swizzle). The caller has waited for
+// the warp's previous store to finish reading the staging area. Returns
+// false when a wait gave up.
+template <int COLS, int OUT_STAGE_BYTES, int GSTRIDE = 64, int GCOLS = 64, int BOXC = 64>
 __device__ __forceinline__ bool store_warp_tile(float (&fin)[COLS], const CUtensorMap& tmap_out, const GemmParams& p,
                                                 const TileCoord& tc, int quarter, int lane, int col0,
                                                 uint8_t* stage_out, uint64_t* oldout_bar, uint32_t& oldout_phase,
                                                 volatile int* abort_flag) {
+  static_assert(BOXC == 64 || BOXC == 32, "bf16 box width");
+  static_assert(GCOLS % BOXC == 0 && GCOLS % 32 == 0, "boxes never straddle a column group");
   const uint32_t stage_addr = smem_u32(stage_out);
   bool ok = true;
   const bool rows_in = (tc.m0 + quarter * 32) < p.m;
   const uint32_t swz = static_cast<uint32_t>(lane & 7);
+  auto colof = [&](int f) -> int { return col0 + (f / GCOLS) * GSTRIDE + (f % GCOLS); };
   // accumulate: the previous output boxes come in through the same tensor
-  // map and 128B-swizzled staging layout the store uses (TMA load into this
+  // map and swizzled staging layout the store uses (TMA load into this
   // warp's staging area, bounded wait), so each thread adds its own row.
-  auto load_previous = [&](int nboxes, int box_cols, int first_box) -> bool {
+  auto load_previous = [&](int nboxes, int box_cols, int box_bytes, int first_box) -> bool {
     if (lane == 0) {
       uint32_t bytes = 0;
-      for (int b = 0; b < nboxes; ++b) bytes += col0 + (first_box + b) * box_cols < p.n ? 4096u : 0u;
+      for (int b = 0; b < nboxes; ++b) bytes += colof((first_box + b) * box_cols) < p.n ? box_bytes : 0u;
       mbar_arrive_expect_tx(oldout_bar, bytes);
       for (int b = 0; b < nboxes; ++b) {
-        const int c = col0 + (first_box + b) * box_cols;
-        if (c < p.n) tma_load_3d(stage_out + b * 4096, &tmap_out, oldout_bar, c, tc.m0 + quarter * 32, tc.e);
+        const int c = colof((first_box + b) * box_cols);
+        if (c < p.n) tma_load_3d(stage_out + b * box_bytes, &tmap_out, oldout_bar, c, tc.m0 + quarter * 32, tc.e);
       }
     }
     const bool landed = mbar_wait(oldout_bar, oldout_phase, abort_flag, kDevTimeoutEpilogue);
@@ -289,47 +312,61 @@ __device__ __forceinline__ bool store_warp_tile(float (&fin)[COLS], const CUtens
     return __all_sync(0xffffffffu, landed);
   };
   if (!p.out_f32) {
-    // bf16: boxes of 32 rows x 64 columns (128 B rows, 128B swizzle), 4 KB each.
-    constexpr int BOXES = COLS / 64;
-    if (p.accumulate && rows_in) {
-      ok = load_previous(BOXES, 64, 0);
-      if (!ok) return false;
+    // bf16: boxes of 32 rows x BOXC columns, BOX_BYTES each, PER_ROUND boxes
+    // per staging round. Row `lane` of a box holds CH 16-byte chunks, chunk c
+    // stored at chunk c ^ (swizzle row bits): 128B swizzle XORs with
+    // lane % 8, 64B swizzle with (lane / 2) % 4.
+    constexpr int BOX_BYTES = 32 * BOXC * 2;
+    constexpr int CH = BOXC / 8;
+    constexpr int BOXES = COLS / BOXC;
+    constexpr int PER_ROUND = OUT_STAGE_BYTES / BOX_BYTES < BOXES ? OUT_STAGE_BYTES / BOX_BYTES : BOXES;
+    const uint32_t rsw = BOXC == 64 ? swz : static_cast<uint32_t>((lane >> 1) & 3);
 #pragma unroll
-      for (int bx = 0; bx < BOXES; ++bx) {
-        const uint32_t box = stage_addr + bx * 4096 + lane * 128;
+    for (int bx0 = 0; bx0 < BOXES; bx0 += PER_ROUND) {
+      if (bx0 > 0) {
+        if (lane == 0) bulk_wait_group_read0();
+        __syncwarp();
+      }
+      if (p.accumulate && rows_in) {
+        ok = load_previous(PER_ROUND, BOXC, BOX_BYTES, bx0);
+        if (!ok) return false;
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const uint4 w = ld_shared_v4(box + ((ch ^ swz) << 4));
-          const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-          float* v = &fin[bx * 64 + ch * 8];
+        for (int bi = 0; bi < PER_ROUND; ++bi) {
+          const uint32_t box = stage_addr + bi * BOX_BYTES + lane * (BOXC * 2);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ww[i]));
-            v[2 * i] += f.x;
-            v[2 * i + 1] += f.y;
+          for (int ch = 0; ch < CH; ++ch) {
+            const uint4 w = ld_shared_v4(box + ((ch ^ rsw) << 4));
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+            float* v = &fin[(bx0 + bi) * BOXC + ch * 8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ww[i]));
+              v[2 * i] += f.x;
+              v[2 * i + 1] += f.y;
+            }
           }
         }
       }
-    }
 #pragma unroll
-    for (int bx = 0; bx < BOXES; ++bx) {
-      const uint32_t box = stage_addr + bx * 4096 + lane * 128;
+      for (int bi = 0; bi < PER_ROUND; ++bi) {
+        const uint32_t box = stage_addr + bi * BOX_BYTES + lane * (BOXC * 2);
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        const float* v = &fin[bx * 64 + ch * 8];
-        st_shared_v4(box + ((ch ^ swz) << 4), pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
-                     pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+        for (int ch = 0; ch < CH; ++ch) {
+          const float* v = &fin[(bx0 + bi) * BOXC + ch * 8];
+          st_shared_v4(box + ((ch ^ rsw) << 4), pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                       pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+        }
       }
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0 && rows_in) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && rows_in) {
 #pragma unroll
-      for (int bx = 0; bx < BOXES; ++bx) {
-        const int c = col0 + bx * 64;
-        if (c < p.n) tma_store_3d(&tmap_out, stage_out + bx * 4096, c, tc.m0 + quarter * 32, tc.e);
+        for (int bi = 0; bi < PER_ROUND; ++bi) {
+          const int c = colof((bx0 + bi) * BOXC);
+          if (c < p.n) tma_store_3d(&tmap_out, stage_out + bi * BOX_BYTES, c, tc.m0 + quarter * 32, tc.e);
+        }
+        bulk_commit_group();
       }
-      bulk_commit_group();
     }
   } else {
     // fp32: boxes of 32 rows x 32 columns, PER_ROUND boxes per staging round.
@@ -342,7 +379,7 @@ __device__ __forceinline__ bool store_warp_tile(float (&fin)[COLS], const CUtens
         __syncwarp();
       }
       if (p.accumulate && rows_in) {
-        ok = load_previous(PER_ROUND, 32, bx0);
+        ok = load_previous(PER_ROUND, 32, 4096, bx0);
         if (!ok) return false;
 #pragma unroll
         for (int bi = 0; bi < PER_ROUND; ++bi) {
@@ -373,7 +410,7 @@ __device__ __forceinline__ bool store_warp_tile(float (&fin)[COLS], const CUtens
       if (lane == 0 && rows_in) {
 #pragma unroll
         for (int bi = 0; bi < PER_ROUND; ++bi) {
-          const int c = col0 + (bx0 + bi) * 32;
+          const int c = colof((bx0 + bi) * 32);
           if (c < p.n) tma_store_3d(&tmap_out, stage_out + bi * 4096, c, tc.m0 + quarter * 32, tc.e);
         }
         bulk_commit_group();
@@ -481,8 +518,9 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
       // rest of the 128-row TMA box belongs to the next expert or the guard).
       const int klen = __ldg(p.k_row_offsets + tc.e + 1) - __ldg(p.k_row_offsets + tc.e);
       const int last_atoms = min(4, max(1, (klen - (nkb - 1) * BK + 31) / 32));
+      const int krot = (WGRAD_KROT && nkb > 1) ? (tc.e + tc.m0 / p.bm + tc.n0 / p.bn) % nkb : 0;
       for (int kb = 0; kb < nkb; ++kb) {
-        const int atoms = kb + 1 == nkb ? last_atoms : BK / 32;
+        const int atoms = (kb + krot == nkb - 1 || kb + krot == 2 * nkb - 1) ? last_atoms : BK / 32;
         // Whole warp waits (keeps the warp converged for the .sync.aligned ops).
         WGRAD_PROF_T(tm0);
         ok = mbar_wait2(&tempty_bar[acc], aphase ^ 1u, &full_bar[stage], phase, abort_flag, kDevTimeoutMma);
@@ -492,7 +530,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        if (lane == 0) {
+        if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) {
           const uint32_t a_addr = smem_u32(s_a + stage * C::A_BYTES);
           const uint32_t b_addr = smem_u32(s_b + stage * C::B_BYTES);
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -579,7 +617,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
           } else {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
+            if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) {
               if (PAIR && rank != 0) mbar_arrive_cluster(tempty_addr0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
               else mbar_arrive(&tempty_bar[acc]);
             }
@@ -605,7 +643,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sempty_bar[sstage]);
+        if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) mbar_arrive(&sempty_bar[sstage]);
         WGRAD_PROF_ADD(kProfEpiPromote, te1);
         WGRAD_PROF_INC(kProfKBlocks);
         acc ^= 1;
@@ -820,7 +858,7 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        if (lane == 0) {
+        if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) {
           const uint32_t a_addr = smem_u32(s_a + stage * C::A_BYTES);
           const uint32_t b_addr = smem_u32(s_b + stage * C::B_BYTES);
           const uint32_t sf_smem = smem_u32(s_sf + sfs * C::SF_STAGE_BYTES);
@@ -843,7 +881,7 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
         if (++sfs == C::SF_STAGES) { sfs = 0; sfphase ^= 1u; }
       }
       if (!ok) break;
-      if (lane == 0) umma_commit(&tfull_bar[acc]);
+      if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) umma_commit(&tfull_bar[acc]);
       __syncwarp();
       acc ^= 1;
       if (acc == 0) aphase ^= 1u;
@@ -899,7 +937,7 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
         WGRAD_PROF_T(tf2);
         fence_proxy_async_smem();  // the copies read through the async proxy
         __syncwarp();
-        if (lane == 0) {
+        if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) {
           mbar_arrive(&sempty_bar[sstage]);
           mbar_arrive(&sffull_bar[sfs]);
         }
@@ -943,7 +981,7 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
         tmem_wait_ld_bind(r1);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) mbar_arrive(&tempty_bar[acc]);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           fin[j] = __uint_as_float(r0[j]);
@@ -979,20 +1017,29 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
 
 }  // namespace
 
+// Raises a kernel's dynamic shared-memory limit once per (kernel, device);
+// thread-safe (a std::once_flag per device ordinal), and every later call on
+// that device returns the first attempt's result.
+template <auto Kernel>
+static cudaError_t configure_once(int smem_bytes) {
+  static std::once_flag flags[kMaxDevices];
+  static cudaError_t result[kMaxDevices];
+  int dev = 0;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::call_once(flags[dev], [&] {
+    result[dev] = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  });
+  return result[dev];
+}
+
 template <int BN, int EPI, bool PAIR = false>
 static cudaError_t launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                                const GemmParams& p, int grid, cudaStream_t stream) {
   using C = Cfg<BN, EPI, PAIR>;
-  static int configured_device_mask = 0;  // bit per device ordinal (< 32)
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
+  const cudaError_t err = configure_once<grouped_wgrad_kernel<BN, EPI, PAIR>>(C::SMEM_BYTES);
   if (err != cudaSuccess) return err;
-  if (dev >= 32 || !(configured_device_mask & (1 << dev))) {
-    err = cudaFuncSetAttribute(grouped_wgrad_kernel<BN, EPI, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               C::SMEM_BYTES);
-    if (err != cudaSuccess) return err;
-    if (dev < 32) configured_device_mask |= (1 << dev);
-  }
   if constexpr (PAIR) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(grid & ~1));  // whole clusters of two
@@ -1014,16 +1061,8 @@ static cudaError_t launch_impl(const CUtensorMap& ta, const CUtensorMap& tb, con
 
 static cudaError_t launch_ue8m0(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                                 const GemmParams& p, int grid, cudaStream_t stream) {
-  static int configured_device_mask = 0;  // bit per device ordinal (< 32)
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
+  const cudaError_t err = configure_once<grouped_wgrad_ue8m0_kernel>(BsCfg::SMEM_BYTES);
   if (err != cudaSuccess) return err;
-  if (dev >= 32 || !(configured_device_mask & (1 << dev))) {
-    err = cudaFuncSetAttribute(grouped_wgrad_ue8m0_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               BsCfg::SMEM_BYTES);
-    if (err != cudaSuccess) return err;
-    if (dev < 32) configured_device_mask |= (1 << dev);
-  }
   grouped_wgrad_ue8m0_kernel<<<grid, BsCfg::THREADS, BsCfg::SMEM_BYTES, stream>>>(ta, tb, to, p);
   return cudaGetLastError();
 }

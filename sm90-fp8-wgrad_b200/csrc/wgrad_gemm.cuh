@@ -8,6 +8,8 @@
 
 namespace wgrad {
 
+constexpr int kMaxDevices = 64;  // device ordinals with per-device launch state
+
 #ifndef WGRAD_PROFILE
 #define WGRAD_PROFILE 0
 #endif

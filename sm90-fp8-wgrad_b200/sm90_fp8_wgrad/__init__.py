@@ -21,7 +21,7 @@ from .checks import (
     scaled_wgrad_error,
     scaled_wgrad_stats,
 )
-from .interface import fp8_grouped_wgrad_sm90, fp8_grouped_wgrad_sm100
+from .interface import check_device_errors, fp8_grouped_wgrad_sm90, fp8_grouped_wgrad_sm100
 from .quant import (
     Fp8GroupedWgradOperand,
     quantize_grouped_wgrad_operand_128x1,
@@ -38,6 +38,7 @@ __all__ = [
     "build_wgrad_full_block_split",
     "build_wgrad_scale_block_meta",
     "build_wgrad_tail_block_meta",
+    "check_device_errors",
     "deepseek_calc_diff",
     "fp8_grouped_wgrad_sm90",
     "fp8_grouped_wgrad_sm100",

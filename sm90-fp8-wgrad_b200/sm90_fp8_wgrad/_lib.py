@@ -37,15 +37,22 @@ TILE_128x192_W12 = 6
 TILE_128x192_UE8M0 = 7
 TILE_256x256_PAIR = 8
 TILE_256x256_PAIR_W16 = 9
+TILE_256x256_SP = 10
+TILE_256x256_SP_W16 = 11
 SCALE_FP32 = 0
 SCALE_UE8M0 = 1
 
 # Every symbol include/sm100_fp8_wgrad.h declares.
 EXPORTED_SYMBOLS = (
     "sm100_fp8_grouped_wgrad",
+    "sm100_wgrad_workspace_bytes",
     "sm100_wgrad_quantize_1x128",
+    "sm100_wgrad_quantize_1x128_ex",
     "sm100_wgrad_build_meta",
     "sm100_wgrad_device_error",
+    "sm100_wgrad_poll_device_error",
+    "sm100_wgrad_build_flags",
+    "sm100_wgrad_profile_counters",
     "sm100_wgrad_status_string",
     "sm100_wgrad_version",
 )
@@ -72,6 +79,8 @@ class Sm100WgradArgs(ctypes.Structure):
         ("expert_order", ctypes.c_void_p),
         ("tile_config", ctypes.c_int32),
         ("max_ctas", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_int64),
     ]
 
 
@@ -148,6 +157,8 @@ def load() -> ctypes.CDLL:
             raise RuntimeError(f"cannot load {path}: {exc}") from exc
         lib.sm100_fp8_grouped_wgrad.argtypes = [ctypes.POINTER(Sm100WgradArgs), ctypes.c_void_p]
         lib.sm100_fp8_grouped_wgrad.restype = ctypes.c_int
+        lib.sm100_wgrad_workspace_bytes.argtypes = [ctypes.POINTER(Sm100WgradArgs), ctypes.POINTER(ctypes.c_int64)]
+        lib.sm100_wgrad_workspace_bytes.restype = ctypes.c_int
         lib.sm100_wgrad_quantize_1x128.argtypes = [
             ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
@@ -164,6 +175,10 @@ def load() -> ctypes.CDLL:
         lib.sm100_wgrad_profile_counters.restype = ctypes.c_int
         lib.sm100_wgrad_device_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
         lib.sm100_wgrad_device_error.restype = ctypes.c_int
+        lib.sm100_wgrad_poll_device_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
+        lib.sm100_wgrad_poll_device_error.restype = ctypes.c_int
+        lib.sm100_wgrad_build_flags.argtypes = []
+        lib.sm100_wgrad_build_flags.restype = ctypes.c_int
         lib.sm100_wgrad_status_string.argtypes = [ctypes.c_int]
         lib.sm100_wgrad_status_string.restype = ctypes.c_char_p
         lib.sm100_wgrad_version.argtypes = []
@@ -204,6 +219,47 @@ def device_error() -> int:
     code = ctypes.c_int32(0)
     check(load().sm100_wgrad_device_error(ctypes.byref(code)), "sm100_wgrad_device_error")
     return int(code.value)
+
+
+DEVICE_ERRORS = {
+    1: "a bounded wait of the GEMM's producer gave up (device-side timeout)",
+    2: "a bounded wait of the GEMM's MMA issuer gave up (device-side timeout)",
+    3: "a bounded wait of the GEMM's promotion/epilogue warps gave up (device-side timeout)",
+    4: "a tile index outside the launch",
+    5: "a quantiser gather index outside [0, x_rows)",
+    6: "an operand labelled UE8M0 carried a scale that is not a positive power of two",
+}
+
+BUILD_DEBUG_MODES = 1
+BUILD_PROFILE = 2
+
+
+def build_flags() -> int:
+    """Compile-time features of the loaded library (BUILD_* bit mask)."""
+    return int(load().sm100_wgrad_build_flags())
+
+
+def poll_device_error() -> int:
+    """Device error recorded by a finished launch since the last poll or read
+    (0 if none), read from a pinned host-mapped word without synchronising."""
+    code = ctypes.c_int32(0)
+    status = load().sm100_wgrad_poll_device_error(ctypes.byref(code))
+    if int(status) == ERR_UNSUPPORTED:
+        return 0
+    check(status, "sm100_wgrad_poll_device_error")
+    return int(code.value)
+
+
+def raise_device_error(code: int, when: str) -> None:
+    if code:
+        what = DEVICE_ERRORS.get(int(code), "unknown device error")
+        raise RuntimeError(f"sm100 Wgrad device error {int(code)} {when}: {what}; the output of that launch is invalid")
+
+
+def raise_pending_device_error() -> None:
+    """Raise RuntimeError if an earlier launch on the current device recorded a
+    device-side error (non-blocking; see poll_device_error)."""
+    raise_device_error(poll_device_error(), "in an earlier launch")
 
 
 def version() -> str:

@@ -66,6 +66,8 @@ TUNED_CONFIGS: dict[str, int] = {
     "sm100_128x192_ue8m0": _lib.TILE_128x192_UE8M0,  # power-of-two scales as tensor-core block scales
     "sm100_256x256_pair": _lib.TILE_256x256_PAIR,    # CTA pair (cta_group::2), half of B per SM
     "sm100_256x256_pair_w16": _lib.TILE_256x256_PAIR_W16,  # the same, 16 promotion warps per CTA
+    "sm100_256x256_sp": _lib.TILE_256x256_SP,  # CTA pair, scale product on the tensor core, one FMA per element
+    "sm100_256x256_sp_w16": _lib.TILE_256x256_SP_W16,  # the same, 16 promotion warps per CTA
 }
 
 
@@ -168,6 +170,11 @@ def fp8_grouped_wgrad_sm90(
     scales applied inside the tensor core instead of a per-block fp32 promotion.
     """
     kernel_mode = _kernel_mode()
+    if kernel_mode != "normal" and not _lib.build_flags() & _lib.BUILD_DEBUG_MODES:
+        raise RuntimeError(
+            f"kernel mode {kernel_mode!r} needs the debug-modes library: build it with "
+            "`python sm90-fp8-wgrad_b200/build_ext.py --debug-modes` and load it with SM100_WGRAD_LIB=<path>"
+        )
     layout_mode = resolve_wgrad_layout_mode()
     _check_fp8_operand("lhs", lhs)
     _check_fp8_operand("rhs", rhs)
@@ -206,6 +213,11 @@ def fp8_grouped_wgrad_sm90(
                 )
             if kd.dtype != torch.float8_e4m3fn or kd.ndim != 2 or int(kd.stride(1)) != 1 or int(kd.stride(0)) % 16:
                 raise RuntimeError(f"packed {name}.kernel_data must be float8_e4m3fn [cols, K] with K contiguous")
+    if int(getattr(meta, "block_k", 128)) != 128:
+        raise RuntimeError(
+            f"metadata block_k must be 128 (the kernel's K block and scale block), got {int(meta.block_k)}; "
+            "tail metadata with 32/64-row blocks feeds quantize_grouped_wgrad_operand_tail_k, not this operator"
+        )
     if lhs.scales.shape[0] != rhs.scales.shape[0]:
         raise RuntimeError("lhs/rhs scale block count mismatch")
     if int(lhs.scales.shape[0]) != int(meta.total_blocks):
@@ -288,15 +300,32 @@ def fp8_grouped_wgrad_sm90(
     args.max_ctas = int(os.environ.get("SM100_WGRAD_MAX_CTAS", "0") or 0)
     lib = _lib.load()
     with torch.cuda.device(dev):
+        # A device-side failure of an earlier launch (bounded wait that gave up,
+        # mislabelled UE8M0 scales, bad gather index) surfaces here, without a sync.
+        _lib.raise_pending_device_error()
+    need = ctypes.c_int64(0)
+    _lib.check(lib.sm100_wgrad_workspace_bytes(ctypes.byref(args), ctypes.byref(need)), "sm100_wgrad_workspace_bytes")
+    workspace = None
+    if need.value > 0:
+        # Scratch for the split scales, from the caching allocator on the
+        # launch stream; it is released when the launch has consumed it.
+        workspace = torch.empty(int(need.value), dtype=torch.uint8, device=dev)
+        args.workspace, args.workspace_bytes = workspace.data_ptr(), int(need.value)
+    with torch.cuda.device(dev):
         status = lib.sm100_fp8_grouped_wgrad(ctypes.byref(args), torch.cuda.current_stream().cuda_stream)
-    if int(status) == _lib.ERR_UNSUPPORTED and kernel_mode != "normal":
-        raise RuntimeError(
-            f"kernel mode {kernel_mode!r} needs the debug-modes library: build it with "
-            "`python sm90-fp8-wgrad_b200/build_ext.py --debug-modes` and load it with SM100_WGRAD_LIB=<path>"
-        )
     _lib.check(status, "sm100_fp8_grouped_wgrad")
     return out
 
 
 # B200-native alias of the same operator.
 fp8_grouped_wgrad_sm100 = fp8_grouped_wgrad_sm90
+
+
+def check_device_errors(device: torch.device | int | None = None) -> None:
+    """Synchronise ``device`` and raise RuntimeError if any launch of this
+    library on it recorded a device-side error (a bounded wait that gave up,
+    a UE8M0-labelled operand whose scales are not powers of two, a quantiser
+    gather index out of range). Clears the error."""
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        torch.cuda.synchronize()
+        _lib.raise_device_error(_lib.device_error(), "recorded on this device")

@@ -188,6 +188,66 @@ def check_sampled_experts(inp, layout: str, with_rel_err: bool = False):
     return (worst, zeros_ok, worst_rel) if with_rel_err else (worst, zeros_ok)
 
 
+def check_all_experts(inp, layout: str) -> dict:
+    """Whole-output correctness, streamed by expert as the reference's benchmark
+    does (scripts/benchmark_wgrad.py:360-414, checks.py:64-86 and :190-223):
+    for every expert of both GEMMs, an fp32 dequantise-then-matmul of the same
+    FP8 operands on the GPU (``float32_matmul_precision("highest")``, no TF32);
+    DeepSeek calc_diff accumulated over all experts of a GEMM, against the
+    reference rounded to the output dtype (the reference's metric) and against
+    the fp32 reference itself; the worst single expert; the normwise max
+    relative error max|out - ref| / max|ref|; every output finite and every
+    empty expert exactly zero. Runs after the timed region."""
+    import torch
+
+    counts = inp.counts
+    cu = (inp.meta.padded_cu_seqlens_k if layout == "padded" else inp.meta.cu_seqlens_k).cpu().tolist()
+    bo = inp.meta.block_offsets.cpu().tolist()
+    prev = torch.get_float32_matmul_precision()
+    torch.set_float32_matmul_precision("highest")
+
+    def deq(op, k0, k1, b0):
+        rows = k1 - k0
+        nb = (rows + 127) // 128
+        return op.data[k0:k1].float() * op.scales[b0:b0 + nb].repeat_interleave(128, dim=0)[:rows]
+
+    res = {"experts_checked": 0, "finite": True, "empty_experts_zero": True, "worst_expert_calc_diff": 0.0,
+           "max_rel_err_normwise": 0.0}
+    try:
+        for name, lhs, rhs, out in (("down", inp.grad_y_q, inp.hidden_q, inp.down_out_bf16),
+                                    ("gate_up", inp.grad_gate_up_q, inp.x_q, inp.gate_up_out_bf16)):
+            num = den = num32 = den32 = 0.0
+            max_abs = max_ref = 0.0
+            for e, c in enumerate(counts):
+                got = out[e].float()
+                if c == 0:
+                    res["empty_experts_zero"] &= not bool(got.any())
+                    continue
+                k0, k1, b0 = cu[e], cu[e + 1], bo[e]
+                ref = deq(lhs, k0, k1, b0).t() @ deq(rhs, k0, k1, b0)
+                if not bool(torch.isfinite(got).all()):
+                    res["finite"] = False
+                ref_r = ref.to(out.dtype).float()
+                xy, xx, yy = (float((got * ref_r).sum()), float((got * got).sum()), float((ref_r * ref_r).sum()))
+                num, den = num + xy, den + xx + yy
+                num32 += float((got.double() * ref.double()).sum())
+                den32 += float((got.double() ** 2).sum() + (ref.double() ** 2).sum())
+                if xx + yy > 0:
+                    res["worst_expert_calc_diff"] = max(res["worst_expert_calc_diff"], 1.0 - 2.0 * xy / (xx + yy))
+                max_abs = max(max_abs, float((got - ref).abs().max()))
+                max_ref = max(max_ref, float(ref.abs().max()))
+                res["experts_checked"] += 1
+                del got, ref, ref_r
+            res[f"{name}_calc_diff"] = 0.0 if den == 0 else 1.0 - 2.0 * num / den
+            res[f"{name}_calc_diff_vs_fp32"] = 0.0 if den32 == 0 else 1.0 - 2.0 * num32 / den32
+            res["max_rel_err_normwise"] = max(res["max_rel_err_normwise"], max_abs / max(max_ref, 1e-30))
+    finally:
+        torch.set_float32_matmul_precision(prev)
+    res["calc_diff_max"] = max(res.get("down_calc_diff", 0.0), res.get("gate_up_calc_diff", 0.0))
+    res["calc_diff_vs_fp32_max"] = max(res.get("down_calc_diff_vs_fp32", 0.0), res.get("gate_up_calc_diff_vs_fp32", 0.0))
+    return res
+
+
 def run_rank(case: Case, routing, expert_range, local_tokens: int, *, seed: int, layout: str, tuned_config: str,
              warmup: int, active: int, repeat: int, device) -> dict:
     """Time and check one EP rank's problem on ``device``."""

@@ -170,6 +170,7 @@ def _quantize(x: torch.Tensor, gather_idx: torch.Tensor | None, meta: WgradScale
     lib = _lib.load()
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream().cuda_stream
+        _lib.raise_pending_device_error()
         _lib.check(lib.sm100_wgrad_quantize_1x128_ex(ctypes.byref(args), stream), "sm100_wgrad_quantize_1x128_ex")
     return Fp8GroupedWgradOperand(q, scales, kernel_data=kernel_q, scale_format=scale_format)
 

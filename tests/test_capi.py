@@ -40,9 +40,11 @@ def test_version_and_status_strings():
 
 
 def test_struct_layout_matches_header():
-    # 19 fields: 8 pointers, 7 int64, 4 int32 (+ padding): offsets fixed by the C ABI
-    assert ctypes.sizeof(_lib.Sm100WgradArgs) == 8 * 8 + 8 * 7 + 4 * 4 + 0
-    assert _lib.Sm100WgradArgs.max_ctas.offset == ctypes.sizeof(_lib.Sm100WgradArgs) - 4
+    # 21 fields: 9 pointers, 8 int64, 4 int32 (+ padding): offsets fixed by the C ABI
+    assert ctypes.sizeof(_lib.Sm100WgradArgs) == 9 * 8 + 8 * 8 + 4 * 4
+    assert _lib.Sm100WgradArgs.max_ctas.offset == ctypes.sizeof(_lib.Sm100WgradArgs) - 20
+    assert _lib.Sm100WgradArgs.workspace.offset == ctypes.sizeof(_lib.Sm100WgradArgs) - 16
+    assert _lib.Sm100WgradArgs.workspace_bytes.offset == ctypes.sizeof(_lib.Sm100WgradArgs) - 8
     assert ctypes.sizeof(_lib.Sm100WgradMetaOut) == 14 * 8
     # Sm100WgradQuantArgs: 18 eight-byte slots (int32 fields padded to 8)
     assert ctypes.sizeof(_lib.Sm100WgradQuantArgs) == 18 * 8

@@ -140,7 +140,7 @@ def test_quantiser_fp32_input_and_odd_columns(cuda_device):
 
 @pytest.mark.parametrize("tuned_config", ["default", "sm100_128x128", "sm100_128x256_w8", "sm100_128x256_w16",
                                           "sm100_128x128_2cta", "sm100_128x192_w12", "sm100_256x256_pair",
-                                          "sm100_256x256_pair_w16"])
+                                          "sm100_256x256_pair_w16", "sm100_256x256_sp", "sm100_256x256_sp_w16"])
 @pytest.mark.parametrize("case", sorted(SMALL_CASES) + ["c1"])
 def test_grouped_wgrad_matches_oracle(cuda_device, case, tuned_config):
     from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
@@ -162,7 +162,7 @@ def test_grouped_wgrad_matches_oracle(cuda_device, case, tuned_config):
 
 
 @pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w8", "sm100_128x256_w16", "sm100_128x128_2cta",
-                                          "sm100_128x192_w12", "sm100_256x256_pair"])
+                                          "sm100_128x192_w12", "sm100_256x256_pair", "sm100_256x256_sp", "sm100_256x256_sp_w16"])
 def test_grouped_wgrad_fp32_out_and_accumulate(cuda_device, tuned_config):
     from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
 
@@ -189,7 +189,7 @@ def test_grouped_wgrad_fp32_out_and_accumulate(cuda_device, tuned_config):
 
 
 @pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_128x192_w12",
-                                          "sm100_256x256_pair"])
+                                          "sm100_256x256_pair", "sm100_256x256_sp", "sm100_256x256_sp_w16"])
 @pytest.mark.parametrize("hidden,inter", [(144, 80), (272, 48), (512, 128)])
 def test_grouped_wgrad_ragged_tiles(cuda_device, hidden, inter, tuned_config):
     """M, N not multiples of the 128 x 256 tile; empty experts; long K."""
@@ -222,8 +222,9 @@ def test_interface_validation_errors(cuda_device):
         fp8_grouped_wgrad_sm90(lhs, rhs, out.transpose(1, 2), meta)
 
 
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_256x256_sp", "sm100_256x256_sp_w16"])
 @pytest.mark.parametrize("splits", [[0, 2, 5, 8], [0, 0, 3, 3, 8], [0, 8]])
-def test_expert_range_launches_equal_full_launch(cuda_device, splits):
+def test_expert_range_launches_equal_full_launch(cuda_device, splits, tuned_config):
     """out[e0:e1] from expert-range launches equals the full launch bit for bit
     (experts are independent); the experts outside a range stay untouched."""
     from sm90_fp8_wgrad import fp8_grouped_wgrad_sm90
@@ -234,10 +235,10 @@ def test_expert_range_launches_equal_full_launch(cuda_device, splits):
     for lk, rk in STAGES.values():
         m, n = ops[lk].data.shape[1], ops[rk].data.shape[1]
         full = torch.empty((e, m, n), device=cuda_device, dtype=torch.bfloat16)
-        fp8_grouped_wgrad_sm90(ops[lk], ops[rk], full, meta)
+        fp8_grouped_wgrad_sm90(ops[lk], ops[rk], full, meta, tuned_config=tuned_config)
         part = torch.full((e, m, n), float("nan"), device=cuda_device, dtype=torch.bfloat16)
         for a, b in zip(splits[:-1], splits[1:]):
-            fp8_grouped_wgrad_sm90(ops[lk], ops[rk], part, meta, expert_range=(a, b))
+            fp8_grouped_wgrad_sm90(ops[lk], ops[rk], part, meta, expert_range=(a, b), tuned_config=tuned_config)
             assert torch.isnan(part[b:].float()).all() or b == e
         assert torch.equal(part.view(torch.int16), full.view(torch.int16))
     with pytest.raises(RuntimeError, match="expert_range"):
@@ -245,7 +246,8 @@ def test_expert_range_launches_equal_full_launch(cuda_device, splits):
 
 
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_128x192_w12"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_128x192_w12",
+                                          "sm100_256x256_sp", "sm100_256x256_sp_w16"])
 def test_accumulate_on_ragged_tiles(cuda_device, tuned_config, out_dtype):
     """out += result where M, N are not multiples of the tile (the previous output
     comes in through TMA boxes that reach past M and N) and experts are empty."""
@@ -300,7 +302,8 @@ def test_legacy_quantiser_entry_point(cuda_device):
 
 @pytest.mark.parametrize("counts", [[0, 0, 0, 0], [300], [(e * 7) % 4 for e in range(1024)]],
                          ids=["all_empty", "one_expert", "1024_tiny_experts"])
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_256x256_pair"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_256x256_pair",
+                                          "sm100_256x256_sp", "sm100_256x256_sp_w16"])
 def test_grouped_wgrad_edge_expert_sets(cuda_device, counts, tuned_config):
     """Every expert empty (no K rows at all: the launch has no operands and writes
     zeros), a single expert, and 1,024 experts of 0-3 rows each."""

@@ -78,6 +78,27 @@ def test_tail_k_bad_index_sets_device_error(cuda_device):
     assert lib.sm100_wgrad_device_error(ctypes.byref(code)) == 0 and code.value == 0
 
 
+def test_tail_k_bad_index_raises_at_next_call(cuda_device):
+    """Without any synchronisation by the caller, the next quantiser call raises."""
+    from sm90_fp8_wgrad import _lib, build_wgrad_tail_block_meta, quantize_grouped_wgrad_operand_tail_k
+
+    _lib.device_error()
+    counts = [40, 10]
+    tm = build_wgrad_tail_block_meta(torch.tensor(_cu(counts), dtype=torch.int32, device=cuda_device),
+                                     tail_block_k=32)
+    x = torch.ones((sum(counts), 32), device=cuda_device, dtype=torch.bfloat16)
+    bad = tm.tail_indices.clone()
+    bad[3] = 10_000
+    quantize_grouped_wgrad_operand_tail_k(x, bad, tm.meta)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="device error 5"):
+        quantize_grouped_wgrad_operand_tail_k(x, tm.tail_indices, tm.meta)
+    assert _lib.device_error() == 5
+    quantize_grouped_wgrad_operand_tail_k(x, tm.tail_indices, tm.meta)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+
+
 def test_tail_k_rejects_bad_arguments(cuda_device):
     from sm90_fp8_wgrad import build_wgrad_tail_block_meta, quantize_grouped_wgrad_operand_tail_k
 

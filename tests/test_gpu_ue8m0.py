@@ -210,3 +210,25 @@ def test_ue8m0_kernel_flags_scales_that_are_not_powers_of_two(cuda_device):
     torch.cuda.synchronize()
     assert _device_error() == 6
     assert _device_error() == 0  # read-and-clear
+
+
+def test_mislabelled_ue8m0_scales_raise(cuda_device):
+    """The error reaches the caller without a synchronisation: the next call of
+    the operator raises, and so does the explicit check."""
+    from sm90_fp8_wgrad import check_device_errors, fp8_grouped_wgrad_sm90
+
+    spec = SMALL_CASES["single"]
+    meta, ops = _gpu_case(spec, cuda_device, scale_format="fp32")
+    lk, rk = STAGES["down"]
+    lhs = dataclasses.replace(ops[lk], scale_format="ue8m0")
+    rhs = dataclasses.replace(ops[rk], scale_format="ue8m0")
+    out = torch.empty((1, lhs.data.shape[1], rhs.data.shape[1]), device=cuda_device, dtype=torch.bfloat16)
+    _device_error()
+    fp8_grouped_wgrad_sm90(lhs, rhs, out, meta)          # auto selects the UE8M0 kernel from the label
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="device error 6"):
+        fp8_grouped_wgrad_sm90(ops[lk], ops[rk], out, meta)
+    with pytest.raises(RuntimeError, match="device error 6"):
+        check_device_errors(cuda_device)
+    fp8_grouped_wgrad_sm90(ops[lk], ops[rk], out, meta)  # reported once: the context is usable
+    check_device_errors(cuda_device)
