@@ -234,22 +234,26 @@ def _host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_reference_sample(workload: str, seed: int, target_s: float, max_experts: int | None = None) -> dict:
+def cpu_reference_sample(workload: str, seed: int, target_s: float, max_experts: int | None = None,
+                         expert_range: tuple[int, int] | None = None) -> dict:
     """Time the reference's CPU algorithm (dequantise + fp32 matmul per 128-row
     block, checks.py:42-61; restated in oracle/) on a bounded sample of the
-    workload: the first experts of the routed problem, down + gate_up, until
-    ~target_s seconds of CPU work. Returns TFLOP/s over the sample."""
+    workload: experts of ``expert_range`` (the whole problem by default; a
+    rank's contiguous shard at N > 1), biggest first, down + gate_up, until
+    ~target_s seconds of CPU work. Returns the rate over the sample and what
+    the sample was (experts, FLOP, seconds)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import wgrad_oracle as O
     from sm90_fp8_wgrad.routing import make_routing
 
     e_all, top_k, h, i, t, route = WORKLOADS[workload]
     routing = make_routing(tokens=t, experts=e_all, top_k=top_k, route=route, seed=seed)
+    e0, e1 = expert_range if expert_range is not None else (0, e_all)
     gen = torch.Generator().manual_seed(seed + 99)
     flops = 0.0
     elapsed = 0.0
     done = 0
-    order = sorted(range(e_all), key=lambda e: -routing.counts[e])  # biggest first: fewer, longer samples
+    order = sorted(range(e0, e1), key=lambda e: -routing.counts[e])  # biggest first: fewer, longer samples
     for e in order:
         c = routing.counts[e]
         if c == 0:
@@ -273,28 +277,41 @@ def cpu_reference_sample(workload: str, seed: int, target_s: float, max_experts:
         "unit": "TFLOP/s",
         "cores": int(torch.get_num_threads()),
         "kind": "port",
-        "sample": f"{done} of {e_all} experts of {workload} (down+gate_up, {flops / 1e9:.0f} GFLOP, "
+        "sample": f"{done} of experts [{e0},{e1}) of {workload} (down+gate_up, {flops / 1e9:.0f} GFLOP, "
                   f"{elapsed:.1f} s, torch fp32 on CPU)",
         "seconds": elapsed,
+        "flops": flops,
+        "experts": done,
     }
 
 
 def run_reference(args) -> None:
+    """The reference's CPU path on the host cores (rank 0 only). A step is a
+    bounded sample of the workload this GPU count gives one GPU (the whole
+    problem at N=1, the first rank's contiguous expert shard at N>1): the
+    biggest experts of that problem until ~cpu_seconds/steps of CPU work.
+    ``steps`` and ``ms_per_step`` describe exactly the timed samples; the
+    time the whole per-GPU problem would take at the measured rate is under
+    ``extrapolated``, a separate key."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
+    from sm90_fp8_wgrad.routing import make_routing, shard_experts
+
     torch.set_num_threads(_host_threads())
-    per_step = []
-    sample = None
+    e_all, top_k, h, i, t, route = WORKLOADS[args.workload]
+    shard = shard_experts(e_all, world, 0)
+    routing = make_routing(tokens=t, experts=e_all, top_k=top_k, route=route, seed=args.seed)
+    shard_flops = 6.0 * h * i * sum(routing.counts[shard[0]:shard[1]])
+    secs, flops, sample = [], [], None
     for s in range(args.warmup + args.steps):
         res = cpu_reference_sample(args.workload, args.seed, target_s=args.cpu_seconds / max(1, args.steps),
-                                   max_experts=None)
+                                   expert_range=shard)
         if s >= args.warmup:
-            per_step.append(res["value"])
+            secs.append(res["seconds"])
+            flops.append(res["flops"])
             sample = res
-    value = sum(per_step) / len(per_step)
-    e_all, top_k, h, i, t, route = WORKLOADS[args.workload]
-    flops_step = 6.0 * h * i * t * top_k
+    value = sum(flops) / sum(secs) / 1e12
     line = {
         "impl": "reference",
         "metric": "grouped Wgrad FP8 TFLOP/s (down + gate_up per step)",
@@ -303,7 +320,9 @@ def run_reference(args) -> None:
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": flops_step / (value * 1e12) * 1e3 if value > 0 else None,
+        "ms_per_step": sum(secs) / len(secs) * 1e3,
+        "step": f"a bounded sample of the per-GPU problem: {sample['experts']} experts of shard "
+                f"[{shard[0]},{shard[1]}), {sample['flops'] / 1e9:.0f} GFLOP per step",
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
@@ -312,8 +331,12 @@ def run_reference(args) -> None:
         "config": workload_config(args.workload, world),
         "cpu_baseline": {k: sample[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "extrapolated": {"full_per_gpu_step_ms": shard_flops / (value * 1e12) * 1e3 if value > 0 else None,
+                         "full_per_gpu_step_gflop": shard_flops / 1e9,
+                         "how": "whole per-GPU problem's FLOP at the measured sample rate (not measured)"},
         "gpu_launches": 0,
     }
+    line["cpu_baseline"]["value"] = value
     print(json.dumps(line), flush=True)
 
 
@@ -363,6 +386,12 @@ def _profile_traffic(workload: str):
         return json.loads(p.read_text()).get(workload)
     except Exception:
         return None
+
+
+def _tensor_rate_tflops(dev, sm_mhz: float) -> float:
+    """Dense FP8 tensor rate of the whole GPU at an SM clock: 8,192 MACs per SM cycle."""
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    return sms * 8192 * 2 * sm_mhz * 1e6 / 1e12
 
 
 def run_ours(args) -> None:
@@ -451,12 +480,14 @@ def run_ours(args) -> None:
         roof = {"bound": "hbm", "kernel": kname, "achieved": gbs,
                 "peak": float(peaks["hbm_gbs"]), "unit": "GB/s", "frac": gbs / float(peaks["hbm_gbs"]),
                 "peak_source": "measured copy bandwidth (MEASURED_PEAKS.json)"}
-    # The committed capture is of the promotion kernel on fp32 scales.
+    # DRAM bytes per gate_up launch from a committed ncu capture of the same
+    # workload (not a counter of this run); the capture is of the 1-GPU launch,
+    # so at N > 1 it is scaled by this rank's share of experts.
     traffic = _profile_traffic(args.workload) if args.scale_format == "fp32" else None
-    # The ncu capture is of the 1-GPU launch; a rank's launch moves its experts' share.
     roof["traffic"] = None if traffic is None else float(traffic) * (e1 - e0) / e_all
-    roof["traffic_unit"] = ("DRAM bytes per gate_up launch (ncu, profiles/grouped_wgrad_kernel_dsv3_32k_launches.md"
-                            + (", scaled by this rank's share of experts)" if world > 1 else ")"))
+    roof["traffic_unit"] = "DRAM bytes per gate_up launch"
+    roof["traffic_source"] = ("committed ncu capture (dram__bytes_read.sum + dram__bytes_write.sum), not measured "
+                              "in this run" + ("; scaled by this rank's share of experts" if world > 1 else ""))
     roof["step_roofline_ms"] = max(t_tc, t_hbm) * 1e3
     roof["step_roofline_frac"] = max(t_tc, t_hbm) * 1e3 / local_ms
 
@@ -467,7 +498,8 @@ def run_ours(args) -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(_host_threads())   # after the GPU timing: all host cores for the CPU leg
         cpu = cpu_reference_sample(args.workload, args.seed, target_s=args.cpu_seconds)
-        cpu.pop("seconds", None)
+        for key in ("seconds", "flops", "experts"):
+            cpu.pop(key, None)
 
     if rank == 0:
         line = {
@@ -490,6 +522,13 @@ def run_ours(args) -> None:
             "stages_tflops": {"down": down_flops_tf, "gate_up": gate_flops_tf},
             "pct_of_fp8_peak": value / world / fp8_peak,
             "pct_of_nominal_fp8": value / world / NOMINAL_FP8_TFLOPS,
+            # The tensor pipe's own rate: 8,192 FP8 MACs per SM cycle (512 cycles per
+            # 128 x 256 x 128 UMMA block, measured by a UMMA microbenchmark) on every
+            # SM, at the boost clock and at the SM clock seen during the timed region.
+            "pct_of_tensor_rate_boost": value / world / _tensor_rate_tflops(dev, float(peaks.get("sm_max_mhz", 1965))),
+            "pct_of_tensor_rate_at_clock": (value / world / _tensor_rate_tflops(dev, clk["sm_mhz"])
+                                            if clk and clk.get("sm_mhz") else None),
+            "tflops_per_gpu_per_ghz": (value / world / (clk["sm_mhz"] / 1000.0) if clk and clk.get("sm_mhz") else None),
             "hbm_gbs_step": step_bytes / (local_ms * 1e-3) / 1e9,
             "roofline": roof,
             "cpu_baseline": cpu,

@@ -522,6 +522,19 @@ int sm100_wgrad_poll_device_error(int32_t* code) {
   return SM100_WGRAD_OK;
 }
 
+#if WGRAD_TRACE
+// Event trace of CTAs 0 and 1 (trace builds only; not part of the product ABI).
+SM100_WGRAD_API int sm100_wgrad_trace_read(uint64_t* out, int32_t n) {
+  if (out == nullptr || n < 0) return SM100_WGRAD_ERR_INVALID_ARG;
+  static unsigned long long buf[2 * wgrad::kTraceBlocks * wgrad::kTraceEvents];
+  if (cudaMemcpyFromSymbol(buf, wgrad::g_wgrad_trace, sizeof(buf)) != cudaSuccess) return SM100_WGRAD_ERR_LAUNCH;
+  for (int i = 0; i < n && i < static_cast<int>(sizeof(buf) / 8); ++i) out[i] = buf[i];
+  static const unsigned long long zero[2 * wgrad::kTraceBlocks * wgrad::kTraceEvents] = {};
+  if (cudaMemcpyToSymbol(wgrad::g_wgrad_trace, zero, sizeof(zero)) != cudaSuccess) return SM100_WGRAD_ERR_LAUNCH;
+  return SM100_WGRAD_OK;
+}
+#endif
+
 int sm100_wgrad_build_flags(void) {
   return (WGRAD_DEBUG_MODES ? SM100_WGRAD_BUILD_DEBUG_MODES : 0) | (WGRAD_PROFILE ? SM100_WGRAD_BUILD_PROFILE : 0);
 }

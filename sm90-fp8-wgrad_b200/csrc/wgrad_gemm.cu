@@ -79,23 +79,31 @@ __device__ unsigned long long g_wgrad_prof[kProfSlots];
 #define WGRAD_PROF_LATENCY(stage) ((void)0)
 #endif
 
+// Event trace of CTAs 0 and 1 over their first kTraceBlocks K blocks (build
+// with -DWGRAD_TRACE=1; read with sm100_wgrad_trace_read in such builds):
+// SM clock64 stamps of the MMA issuer's and the first promotion warp's steps.
+#ifndef WGRAD_TRACE
+#define WGRAD_TRACE 0
+#endif
+constexpr int kTraceBlocks = 64, kTraceEvents = 8;
+enum TraceEv : int { kTrMmaReady = 0, kTrMmaIssued = 1, kTrEpiWaitStart = 2, kTrEpiReady = 3, kTrEpiReleased = 4,
+                     kTrEpiDone = 5, kTrMmaHalfReady = 6, kTrMmaHalfIssued = 7 };
+#if WGRAD_TRACE
+__device__ unsigned long long g_wgrad_trace[2][kTraceBlocks][kTraceEvents];
+#define WGRAD_TRACE_EV(ev, b)                                                                   \
+  do {                                                                                          \
+    if (blockIdx.x < 2 && (b) < kTraceBlocks && (threadIdx.x & 31) == 0)                        \
+      g_wgrad_trace[blockIdx.x][(b)][(ev)] = static_cast<unsigned long long>(clock64());        \
+  } while (0)
+#else
+#define WGRAD_TRACE_EV(ev, b) ((void)0)
+#endif
+
 namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // scale block == K block, bytes per row of an FP8 tile
 constexpr int SCALE_STAGES = 6;
-#ifndef WGRAD_PAIR_STAGES
-#define WGRAD_PAIR_STAGES 4
-#endif
-#ifndef WGRAD_PAIR_OUT_STAGE
-#define WGRAD_PAIR_OUT_STAGE 8192
-#endif
-#ifndef WGRAD_MMA_ELECT
-#define WGRAD_MMA_ELECT 1  // issue UMMAs from an elect.sync-chosen lane (measured faster than lane == 0)
-#endif
-#ifndef WGRAD_KROT
-#define WGRAD_KROT 0
-#endif
 constexpr int FIRST_EPI_WARP = 4;
 
 // Promotion warps: EPI = 4, 8 or 16 (one, two or four per TMEM lane quarter);
@@ -117,7 +125,7 @@ struct Cfg {
   static constexpr int THREADS = 32 * (4 + EPI_WARPS);
   static constexpr int CTAS_PER_SM = EPI_WARPS == 4 ? 2 : 1;
   // A pair CTA holds half of B, so a stage is 32 KB instead of 48 KB.
-  static constexpr int STAGES = PAIR ? WGRAD_PAIR_STAGES : (EPI_WARPS == 4 ? 2 : 3);
+  static constexpr int STAGES = PAIR ? 4 : (EPI_WARPS == 4 ? 2 : 3);
   static constexpr uint32_t REGS_CONTROL = EPI_WARPS == 16 ? 32 : (EPI_WARPS == 12 ? 40 : 56);
   static constexpr uint32_t REGS_EPILOGUE =
       EPI_WARPS == 16 ? 112 : (EPI_WARPS == 12 ? 152 : (EPI_WARPS == 4 ? 200 : 224));
@@ -125,16 +133,17 @@ struct Cfg {
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows of B this CTA loads
   static constexpr int B_BYTES = B_ROWS * BK;
   static constexpr int SCALE_FLOATS = BM + BN;
+  static constexpr int SSTAGES = SCALE_STAGES;  // scale-vector ring depth
   static constexpr int COLS_PER_WARP = BN / (EPI_WARPS / 4);  // EPI_WARPS / 4 column groups
   // tcgen05.ld columns per load: 32 when two such buffers fit beside the accumulator
   static constexpr int CHUNK = REGS_EPILOGUE >= COLS_PER_WARP + 80 ? 32 : 16;
   static constexpr int CHUNKS = COLS_PER_WARP / CHUNK;
   static constexpr int OUT_STAGE_BYTES_PER_WARP =
-      PAIR ? WGRAD_PAIR_OUT_STAGE : (COLS_PER_WARP * 32 * 2 >= 8192 ? 8192 : 4096);
+      COLS_PER_WARP * 32 * 2 >= 8192 ? 8192 : 4096;
   // double-buffered partial, allocated as a power of two (192-wide tiles use 384 of 512)
   static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
   static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + EPI_WARPS * OUT_STAGE_BYTES_PER_WARP +
-                                    SCALE_STAGES * SCALE_FLOATS * 4 + 512 /*barriers*/ + 1024 /*align*/;
+                                    SSTAGES * SCALE_FLOATS * 4 + 512 /*barriers*/ + 1024 /*align*/;
   static_assert(128 * REGS_CONTROL + 32 * EPI_WARPS * REGS_EPILOGUE <=
                     THREADS * ((65536 / (THREADS * CTAS_PER_SM)) & ~7),
                 "register split exceeds the launch allocation");
@@ -214,9 +223,7 @@ __device__ __forceinline__ void run_producer(const CUtensorMap& tmap_a, const CU
     // the odd CTA of a pair may lie wholly below the last row of M
     const uint32_t a_scale_bytes = static_cast<uint32_t>(max(0, min(BM, p.m - tc.m0))) * 4u;
     const uint32_t b_scale_bytes = static_cast<uint32_t>(min(BN, p.n - tc.n0)) * 4u;
-    const int krot = (WGRAD_KROT && nkb > 1) ? (tc.e + tc.m0 / p.bm + tc.n0 / p.bn) % nkb : 0;
-    for (int kb_i = 0; kb_i < nkb && ok; ++kb_i) {
-      const int kb = kb_i + krot < nkb ? kb_i + krot : kb_i + krot - nkb;
+    for (int kb = 0; kb < nkb && ok; ++kb) {
       WGRAD_PROF_T(tw0);
       ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, kDevTimeoutProducer);
       WGRAD_PROF_ADD(kProfProducerWaitStage, tw0);
@@ -225,7 +232,7 @@ __device__ __forceinline__ void run_producer(const CUtensorMap& tmap_a, const CU
       // Test-only failure injection: announce the first stage's bytes but
       // issue no copy, so the stage never fills and the bounded waits of
       // the consumers expire (device error word, clean exit).
-      const bool withhold = p.inject == kInjectWithholdFirstLoad && tile == tile_begin && kb_i == 0;
+      const bool withhold = p.inject == kInjectWithholdFirstLoad && tile == tile_begin && kb == 0;
       if constexpr (PAIR) {
         const uint32_t leader_full = cluster_addr(&full_bar[stage], 0);
         if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * (C::A_BYTES + C::B_BYTES));
@@ -252,7 +259,7 @@ __device__ __forceinline__ void run_producer(const CUtensorMap& tmap_a, const CU
       mbar_arrive_expect_tx(&sfull_bar[sstage], a_scale_bytes + b_scale_bytes);
       if (a_scale_bytes > 0) bulk_load_1d(dst, p.sa + blk * p.m + tc.m0, a_scale_bytes, &sfull_bar[sstage]);
       bulk_load_1d(dst + BM, p.sb + blk * p.n + tc.n0, b_scale_bytes, &sfull_bar[sstage]);
-      if (++sstage == SCALE_STAGES) { sstage = 0; sphase ^= 1u; }
+      if (++sstage == C::SSTAGES) { sstage = 0; sphase ^= 1u; }
     }
   }
   if constexpr (PAIR) {
@@ -436,12 +443,12 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
   uint8_t* s_b = s_a + C::STAGES * C::A_BYTES;
   uint8_t* s_out = s_b + C::STAGES * C::B_BYTES;
   float* s_scale = reinterpret_cast<float*>(s_out + C::EPI_WARPS * C::OUT_STAGE_BYTES_PER_WARP);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_scale + SCALE_STAGES * C::SCALE_FLOATS);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_scale + C::SSTAGES * C::SCALE_FLOATS);
   uint64_t* full_bar = bars;                          // [C::STAGES]   TMA -> MMA
   uint64_t* empty_bar = full_bar + C::STAGES;            // [C::STAGES]   MMA -> TMA
-  uint64_t* sfull_bar = empty_bar + C::STAGES;           // [SCALE_STAGES] TMA -> epilogue
-  uint64_t* sempty_bar = sfull_bar + SCALE_STAGES;    // [SCALE_STAGES] epilogue -> TMA
-  uint64_t* tfull_bar = sempty_bar + SCALE_STAGES;    // [2] MMA -> epilogue
+  uint64_t* sfull_bar = empty_bar + C::STAGES;           // [C::SSTAGES] TMA -> epilogue
+  uint64_t* sempty_bar = sfull_bar + C::SSTAGES;    // [C::SSTAGES] epilogue -> TMA
+  uint64_t* tfull_bar = sempty_bar + C::SSTAGES;    // [2] MMA -> epilogue
   uint64_t* tempty_bar = tfull_bar + 2;               // [2] epilogue -> MMA
   uint64_t* oldout_bar = tempty_bar + 2;             // [EPI_WARPS] previous output -> promotion warp (accumulate)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(oldout_bar + C::EPI_WARPS);
@@ -465,7 +472,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
       mbar_init(&full_bar[i], 1);
       mbar_init(&empty_bar[i], 1);
     }
-    for (int i = 0; i < SCALE_STAGES; ++i) {
+    for (int i = 0; i < C::SSTAGES; ++i) {
       mbar_init(&sfull_bar[i], 1);
       mbar_init(&sempty_bar[i], C::EPI_WARPS);
     }
@@ -496,6 +503,9 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
   if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+#if WGRAD_PROFILE
+  const long long t_cta0 = clock64();
+#endif
 
   if (warp < FIRST_EPI_WARP) setmaxnreg_dec<C::REGS_CONTROL>();
 
@@ -507,6 +517,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
   } else if (warp == 1 && rank == 0) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc = umma_idesc_e4m3_f32(PAIR ? 2 * BM : BM, BN);
+    int trace_b = 0;
     int stage = 0, acc = 0;
     uint32_t phase = 0, aphase = 0;
     bool ok = true;
@@ -518,9 +529,8 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
       // rest of the 128-row TMA box belongs to the next expert or the guard).
       const int klen = __ldg(p.k_row_offsets + tc.e + 1) - __ldg(p.k_row_offsets + tc.e);
       const int last_atoms = min(4, max(1, (klen - (nkb - 1) * BK + 31) / 32));
-      const int krot = (WGRAD_KROT && nkb > 1) ? (tc.e + tc.m0 / p.bm + tc.n0 / p.bn) % nkb : 0;
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int atoms = (kb + krot == nkb - 1 || kb + krot == 2 * nkb - 1) ? last_atoms : BK / 32;
+      for (int kb = 0; kb < nkb; ++kb, ++trace_b) {
+        const int atoms = kb + 1 == nkb ? last_atoms : BK / 32;
         // Whole warp waits (keeps the warp converged for the .sync.aligned ops).
         WGRAD_PROF_T(tm0);
         ok = mbar_wait2(&tempty_bar[acc], aphase ^ 1u, &full_bar[stage], phase, abort_flag, kDevTimeoutMma);
@@ -529,8 +539,11 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
         WGRAD_PROF_T(tm1);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
+#if WGRAD_TRACE == 1
+        WGRAD_TRACE_EV(kTrMmaReady, trace_b);
+#endif
         tc_fence_after();
-        if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) {
+        if (elect_one_sync()) {
           const uint32_t a_addr = smem_u32(s_a + stage * C::A_BYTES);
           const uint32_t b_addr = smem_u32(s_b + stage * C::B_BYTES);
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -557,6 +570,9 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
           }
         }
         __syncwarp();
+#if WGRAD_TRACE == 1
+        WGRAD_TRACE_EV(kTrMmaIssued, trace_b);
+#endif
         WGRAD_PROF_ADD(kProfMmaIssue, tm1);
         if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         acc ^= 1;
@@ -578,6 +594,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
     bool ok = true;
     // the partial's release goes to the pair's even CTA
     const uint32_t tempty_addr0 = PAIR ? cluster_addr(&tempty_bar[0], 0) : 0u;
+    int trace_b = 0;
     for (int tile = tile_begin; tile < p.num_tiles && ok; tile += tile_stride) {
       const TileCoord tc = decode_tile(p, tile, row_off);
       const int nkb = __ldg(p.block_offsets + tc.e + 1) - __ldg(p.block_offsets + tc.e);
@@ -585,13 +602,15 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
 #pragma unroll
       for (int j = 0; j < C::COLS_PER_WARP; ++j) fin[j] = 0.f;
 
-      for (int kb = 0; kb < nkb; ++kb) {
+      for (int kb = 0; kb < nkb; ++kb, ++trace_b) {
+        if (ew == 0) WGRAD_TRACE_EV(WGRAD_TRACE == 2 ? 7 : kTrEpiWaitStart, trace_b);
         WGRAD_PROF_T(te0);
         ok = mbar_wait2(&tfull_bar[acc], aphase, &sfull_bar[sstage], sphase, abort_flag, kDevTimeoutEpilogue);
         WGRAD_PROF_ADD(kProfEpiWait, te0);
         WGRAD_PROF_T(te1);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
+        if (ew == 0) WGRAD_TRACE_EV(WGRAD_TRACE == 2 ? 0 : kTrEpiReady, trace_b);
         tc_fence_after();
         const float* sc = s_scale + sstage * C::SCALE_FLOATS;
 #if WGRAD_DEBUG_MODES
@@ -612,15 +631,19 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
 #pragma unroll
         for (int c = 0; c < C::CHUNKS; ++c) {
           tmem_wait_ld_bind(r[c & 1]);
+#if WGRAD_TRACE == 2
+          if (ew == 0 && c < 4) WGRAD_TRACE_EV(1 + c, trace_b);
+#endif
           if (c + 1 < C::CHUNKS) {
             tmem_ld_chunk(t_addr + (c + 1) * CH, r[(c + 1) & 1]);
           } else {
             tc_fence_before();
             __syncwarp();
-            if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) {
+            if (lane == 0) {
               if (PAIR && rank != 0) mbar_arrive_cluster(tempty_addr0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
               else mbar_arrive(&tempty_bar[acc]);
             }
+            if (ew == 0) WGRAD_TRACE_EV(WGRAD_TRACE == 2 ? 5 : kTrEpiReleased, trace_b);
           }
 #pragma unroll
           for (int j = 0; j < CH; j += 4) {
@@ -643,12 +666,13 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
           }
         }
         __syncwarp();
-        if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) mbar_arrive(&sempty_bar[sstage]);
+        if (lane == 0) mbar_arrive(&sempty_bar[sstage]);
+        if (ew == 0) WGRAD_TRACE_EV(WGRAD_TRACE == 2 ? 6 : kTrEpiDone, trace_b);
         WGRAD_PROF_ADD(kProfEpiPromote, te1);
         WGRAD_PROF_INC(kProfKBlocks);
         acc ^= 1;
         if (acc == 0) aphase ^= 1u;
-        if (++sstage == SCALE_STAGES) { sstage = 0; sphase ^= 1u; }
+        if (++sstage == C::SSTAGES) { sstage = 0; sphase ^= 1u; }
       }
       if (!ok) break;
 
@@ -685,7 +709,10 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
   __syncthreads();
   if constexpr (PAIR) cluster_sync();  // no cross-CTA arrival or UMMA is left in flight
 #if WGRAD_PROFILE
-  if (threadIdx.x < kProfSlots) atomicAdd(&g_wgrad_prof[threadIdx.x], s_prof[threadIdx.x]);
+  if (threadIdx.x < kProfSlots)
+    atomicAdd(&g_wgrad_prof[threadIdx.x], threadIdx.x == kProfCtaCycles
+                                              ? static_cast<unsigned long long>(clock64() - t_cta0)
+                                              : s_prof[threadIdx.x]);
 #endif
   if (warp == 1) {
     tc_fence_after();
@@ -724,6 +751,7 @@ struct BsCfg {
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int SCALE_FLOATS = BM + BN;
+  static constexpr int SSTAGES = 6;  // scale-vector ring depth
   static constexpr int OUT_STAGE_BYTES_PER_WARP = 4096;
   static constexpr int SF_STAGES = 4;
   static constexpr int SF_A_BYTES = 512;    // 128 rows
@@ -734,7 +762,7 @@ struct BsCfg {
   static constexpr int SF_B_OFFSET = 4;
   static constexpr int TMEM_COLS = 512;
   static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + EPI_WARPS * OUT_STAGE_BYTES_PER_WARP +
-                                    SF_STAGES * SF_STAGE_BYTES + SCALE_STAGES * SCALE_FLOATS * 4 +
+                                    SF_STAGES * SF_STAGE_BYTES + SSTAGES * SCALE_FLOATS * 4 +
                                     512 /*barriers*/ + 1024 /*align*/;
   static_assert(SF_COL0 + SF_STAGES * SF_STAGE_COLS <= TMEM_COLS, "TMEM columns");
   static_assert(COLS_PER_WARP * 32 * 2 == OUT_STAGE_BYTES_PER_WARP, "one BF16 staging round per tile");
@@ -765,12 +793,12 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
   uint8_t* s_out = s_b + C::STAGES * C::B_BYTES;
   uint8_t* s_sf = s_out + C::EPI_WARPS * C::OUT_STAGE_BYTES_PER_WARP;    // [SF_STAGES][A 512 | B 1024]
   float* s_scale = reinterpret_cast<float*>(s_sf + C::SF_STAGES * C::SF_STAGE_BYTES);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_scale + SCALE_STAGES * C::SCALE_FLOATS);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_scale + C::SSTAGES * C::SCALE_FLOATS);
   uint64_t* full_bar = bars;                             // [STAGES]      TMA -> MMA
   uint64_t* empty_bar = full_bar + C::STAGES;            // [STAGES]      MMA -> TMA
-  uint64_t* sfull_bar = empty_bar + C::STAGES;           // [SCALE_STAGES] TMA -> SF writer
-  uint64_t* sempty_bar = sfull_bar + SCALE_STAGES;       // [SCALE_STAGES] SF writer -> TMA
-  uint64_t* sffull_bar = sempty_bar + SCALE_STAGES;      // [SF_STAGES]   SF writer -> MMA
+  uint64_t* sfull_bar = empty_bar + C::STAGES;           // [C::SSTAGES] TMA -> SF writer
+  uint64_t* sempty_bar = sfull_bar + C::SSTAGES;       // [C::SSTAGES] SF writer -> TMA
+  uint64_t* sffull_bar = sempty_bar + C::SSTAGES;      // [SF_STAGES]   SF writer -> MMA
   uint64_t* sfempty_bar = sffull_bar + C::SF_STAGES;     // [SF_STAGES]   MMA (copies done) -> SF writer
   uint64_t* tfull_bar = sfempty_bar + C::SF_STAGES;      // [2] MMA -> epilogue
   uint64_t* tempty_bar = tfull_bar + 2;                  // [2] epilogue -> MMA
@@ -795,7 +823,7 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
       mbar_init(&full_bar[i], 1);
       mbar_init(&empty_bar[i], 1);
     }
-    for (int i = 0; i < SCALE_STAGES; ++i) {
+    for (int i = 0; i < C::SSTAGES; ++i) {
       mbar_init(&sfull_bar[i], 1);
       mbar_init(&sempty_bar[i], 1);
     }
@@ -824,6 +852,9 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+#if WGRAD_PROFILE
+  const long long t_cta0 = clock64();
+#endif
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -858,7 +889,7 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) {
+        if (elect_one_sync()) {
           const uint32_t a_addr = smem_u32(s_a + stage * C::A_BYTES);
           const uint32_t b_addr = smem_u32(s_b + stage * C::B_BYTES);
           const uint32_t sf_smem = smem_u32(s_sf + sfs * C::SF_STAGE_BYTES);
@@ -881,7 +912,7 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
         if (++sfs == C::SF_STAGES) { sfs = 0; sfphase ^= 1u; }
       }
       if (!ok) break;
-      if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) umma_commit(&tfull_bar[acc]);
+      if (elect_one_sync()) umma_commit(&tfull_bar[acc]);
       __syncwarp();
       acc ^= 1;
       if (acc == 0) aphase ^= 1u;
@@ -937,14 +968,14 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
         WGRAD_PROF_T(tf2);
         fence_proxy_async_smem();  // the copies read through the async proxy
         __syncwarp();
-        if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) {
+        if (elect_one_sync()) {
           mbar_arrive(&sempty_bar[sstage]);
           mbar_arrive(&sffull_bar[sfs]);
         }
         WGRAD_PROF_ADD(kProfSfPublish, tf2);
         WGRAD_PROF_ADD(kProfEpiPromote, tf1);
         WGRAD_PROF_INC(kProfKBlocks);
-        if (++sstage == SCALE_STAGES) { sstage = 0; sphase ^= 1u; }
+        if (++sstage == C::SSTAGES) { sstage = 0; sphase ^= 1u; }
         if (++sfs == C::SF_STAGES) { sfs = 0; sfphase ^= 1u; }
       }
     }
@@ -981,7 +1012,7 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
         tmem_wait_ld_bind(r1);
         tc_fence_before();
         __syncwarp();
-        if (WGRAD_MMA_ELECT ? elect_one_sync() : lane == 0) mbar_arrive(&tempty_bar[acc]);
+        if (elect_one_sync()) mbar_arrive(&tempty_bar[acc]);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           fin[j] = __uint_as_float(r0[j]);
@@ -1007,7 +1038,10 @@ __global__ void __launch_bounds__(BsCfg::THREADS, 1)
   tc_fence_before();
   __syncthreads();
 #if WGRAD_PROFILE
-  if (threadIdx.x < kProfSlots) atomicAdd(&g_wgrad_prof[threadIdx.x], s_prof[threadIdx.x]);
+  if (threadIdx.x < kProfSlots)
+    atomicAdd(&g_wgrad_prof[threadIdx.x], threadIdx.x == kProfCtaCycles
+                                              ? static_cast<unsigned long long>(clock64() - t_cta0)
+                                              : s_prof[threadIdx.x]);
 #endif
   if (warp == 1) {
     tc_fence_after();

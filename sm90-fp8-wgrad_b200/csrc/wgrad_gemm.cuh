@@ -33,6 +33,7 @@ enum ProfSlot : int {
   kProfSfSync = 14,             // UE8M0 scale-factor writer: warp vote after its barrier wait
   kProfSfLoad = 15,             // UE8M0 scale-factor writer: scale loads and E8M0 conversion
   kProfMmaTileWait = 16,        // UE8M0 MMA warp: wait for a free accumulator at a tile's start
+  kProfCtaCycles = 17,          // whole CTA: cycles from the end of set-up to the final barrier
   kProfSlots = 24,
 };
 

@@ -58,33 +58,7 @@ namespace wgrad {
 
 namespace {
 
-#ifndef WGRAD_SP_STAGES
-#define WGRAD_SP_STAGES 4
-#endif
-#ifndef WGRAD_SP_REGS_CONTROL
-#define WGRAD_SP_REGS_CONTROL 56
-#endif
-#ifndef WGRAD_SP_REGS_EPILOGUE
-#define WGRAD_SP_REGS_EPILOGUE 224
-#endif
-#ifndef WGRAD_SP_FMA2
-#define WGRAD_SP_FMA2 1
-#endif
-#ifndef WGRAD_SP_ELECT
-#define WGRAD_SP_ELECT 1
-#endif
-#ifndef WGRAD_SP_EXP
-#define WGRAD_SP_EXP 0  // experiment switches (timing only): 1 no S loads, 2 no TMEM loads, 4 no TMA loads
-#endif
-#ifndef WGRAD_SP_SKIP_S
-#define WGRAD_SP_SKIP_S 0
-#endif
-#ifndef SP_CHUNK
-#define SP_CHUNK 16
-#endif
-#ifndef WGRAD_SP_OUT_STAGE
-#define WGRAD_SP_OUT_STAGE 8192
-#endif
+constexpr int SP_CHUNK = 16;  // TMEM columns of P (and of S) per tcgen05.ld round trip
 
 template <int EPI>
 struct SpCfg {
@@ -92,7 +66,7 @@ struct SpCfg {
   static constexpr int BN = 256;            // columns per tile
   static constexpr int HALF = 128;          // columns per TMEM slot (UMMA N)
   static constexpr int BK = 128;            // K block = scale block
-  static constexpr int STAGES = WGRAD_SP_STAGES;
+  static constexpr int STAGES = 4;
   static constexpr int EPI_WARPS = EPI;     // promotion warps: 8 (2 per TMEM lane quarter) or 16 (4)
   static constexpr int FIRST_EPI = 4;
   static constexpr int THREADS = 32 * (FIRST_EPI + EPI_WARPS);
@@ -106,11 +80,11 @@ struct SpCfg {
   static constexpr int SB_HALF_BYTES = (HALF / 2) * 32;  // 2 KB
   static constexpr int SB_BYTES = 2 * SB_HALF_BYTES;
   static constexpr int STAGE_TX = A_BYTES + B_BYTES + SA_BYTES + SB_BYTES;  // per CTA
-  static constexpr int OUT_STAGE_BYTES_PER_WARP = EPI == 16 ? 4096 : WGRAD_SP_OUT_STAGE;
+  static constexpr int OUT_STAGE_BYTES_PER_WARP = EPI == 16 ? 4096 : 8192;
   // setmaxnreg split of the launch's registers (threads x regs at launch):
   // 8 warps: 384 x 168 >= 128 x 56 + 256 x 224; 16 warps: 640 x 96 = 128 x 32 + 512 x 112.
-  static constexpr uint32_t REGS_CONTROL = EPI == 16 ? 32 : WGRAD_SP_REGS_CONTROL;
-  static constexpr uint32_t REGS_EPILOGUE = EPI == 16 ? 112 : WGRAD_SP_REGS_EPILOGUE;
+  static constexpr uint32_t REGS_CONTROL = EPI == 16 ? 32 : 56;
+  static constexpr uint32_t REGS_EPILOGUE = EPI == 16 ? 112 : 224;
   static constexpr int TMEM_COLS = 512;
   static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES + SA_BYTES + SB_BYTES) +
                                     EPI_WARPS * OUT_STAGE_BYTES_PER_WARP + 512 /*barriers*/ + 1024 /*align*/;
@@ -188,6 +162,9 @@ __global__ void __launch_bounds__(SpCfg<EPI>::THREADS, 1)
   cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+#if WGRAD_PROFILE
+  const long long t_cta0 = clock64();
+#endif
 
   if (warp < C::FIRST_EPI) setmaxnreg_dec<C::REGS_CONTROL>();
 
@@ -218,8 +195,8 @@ __global__ void __launch_bounds__(SpCfg<EPI>::THREADS, 1)
 #endif
           const bool withhold = p.inject == kInjectWithholdFirstLoad && r == 0 && kb == 0;
           const uint32_t lf = leader_full0 + static_cast<uint32_t>(stage * sizeof(uint64_t));
-          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], (WGRAD_SP_EXP & 4) ? 0u : 2 * C::STAGE_TX);
-          if (!withhold && !(WGRAD_SP_EXP & 4)) {
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * C::STAGE_TX);
+          if (!withhold) {
             const int kc = krow0 + kb * C::BK;
             const int blk = kb0 + kb;
             uint8_t* b_dst = s_b + stage * C::B_BYTES;
@@ -256,7 +233,7 @@ __global__ void __launch_bounds__(SpCfg<EPI>::THREADS, 1)
     // shared::cluster addresses of the barriers in CTA 0 and CTA 1
     const uint32_t tfull_c0 = cluster_addr(&tfull_bar[0], 0), tfull_c1 = cluster_addr(&tfull_bar[0], 1);
     const uint32_t empty_c0 = cluster_addr(&empty_bar[0], 0), empty_c1 = cluster_addr(&empty_bar[0], 1);
-    int stage = 0;
+    int stage = 0, trace_b = 0;
     uint32_t phase = 0, aphase = 0;
     bool ok = true;
     for (int r = 0; r < rounds && ok; ++r) {
@@ -268,16 +245,6 @@ __global__ void __launch_bounds__(SpCfg<EPI>::THREADS, 1)
       const int klen = __ldg(p.k_row_offsets + tc.e + 1) - __ldg(p.k_row_offsets + tc.e);
       const int last_atoms = min(4, max(1, (klen - (nkb - 1) * C::BK + 31) / 32));
       for (int kb = 0; kb < nkb && ok; ++kb) {
-        if (WGRAD_SP_EXP & 8) {  // delivery only: release each stage as soon as it is full
-          ok = mbar_wait(&full_bar[stage], phase, abort_flag, kDevTimeoutMma);
-          if (elect_one_sync()) {
-            mbar_arrive(&empty_bar[stage]);
-            mbar_arrive_cluster(cluster_addr(&empty_bar[stage], 1));
-          }
-          __syncwarp();
-          if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
-          continue;
-        }
         const int atoms = kb + 1 == nkb ? last_atoms : C::BK / 32;
         const uint64_t da = da0 + static_cast<uint64_t>((stage * C::A_BYTES) >> 4);
         const uint64_t dsa = dsa0 + static_cast<uint64_t>((stage * C::SA_BYTES) >> 4);
@@ -293,16 +260,16 @@ __global__ void __launch_bounds__(SpCfg<EPI>::THREADS, 1)
           WGRAD_PROF_T(tm1);
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
+          WGRAD_TRACE_EV(h == 0 ? kTrMmaReady : kTrMmaHalfReady, trace_b);
           tc_fence_after();
-          if (WGRAD_SP_ELECT ? elect_one_sync() : lane == 0) {
+          if (elect_one_sync()) {
             const uint64_t db = db0 + static_cast<uint64_t>((stage * C::B_BYTES + h * C::B_HALF_BYTES) >> 4);
             const uint32_t d_p = tmem_base + static_cast<uint32_t>(h * 2 * C::HALF);
             umma_f8_pair(d_p, da, db, idesc_p, 0u);
             if (atoms > 1) umma_f8_pair(d_p, da + 2, db + 2, idesc_p, 1u);
             if (atoms > 2) umma_f8_pair(d_p, da + 4, db + 4, idesc_p, 1u);
             if (atoms > 3) umma_f8_pair(d_p, da + 6, db + 6, idesc_p, 1u);
-            if (!WGRAD_SP_SKIP_S)
-              umma_tf32_pair(d_p + C::HALF, dsa, dsb0 + static_cast<uint64_t>((stage * C::SB_BYTES + h * C::SB_HALF_BYTES) >> 4),
+            umma_tf32_pair(d_p + C::HALF, dsa, dsb0 + static_cast<uint64_t>((stage * C::SB_BYTES + h * C::SB_HALF_BYTES) >> 4),
                              idesc_s, 0u);
             // the partial is ready in both CTAs; after the second half the stage is free in both
             const uint32_t th = static_cast<uint32_t>(h * sizeof(uint64_t));
@@ -315,10 +282,12 @@ __global__ void __launch_bounds__(SpCfg<EPI>::THREADS, 1)
             }
           }
           __syncwarp();
+          WGRAD_TRACE_EV(h == 0 ? kTrMmaIssued : kTrMmaHalfIssued, trace_b);
           WGRAD_PROF_ADD(kProfMmaIssue, tm1);
         }
         if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         aphase ^= 1u;
+        ++trace_b;
       }
     }
   } else if (warp >= C::FIRST_EPI) {
@@ -331,6 +300,7 @@ __global__ void __launch_bounds__(SpCfg<EPI>::THREADS, 1)
     uint8_t* stage_out = s_out + ew * C::OUT_STAGE_BYTES_PER_WARP;
     const uint32_t tempty_leader0 = cluster_addr(&tempty_bar[0], 0);
     uint32_t aphase = 0, oldout_phase = 0;
+    int trace_b = 0;
     bool ok = true;
 #if WGRAD_DEBUG_MODES
     const bool unit_scales = p.mode == kModeUnscaled;  // raw FP8 product only
@@ -345,24 +315,26 @@ __global__ void __launch_bounds__(SpCfg<EPI>::THREADS, 1)
 #pragma unroll
       for (int j = 0; j < C::COLS_PER_WARP; ++j) fin[j] = 0.f;
 
-      for (int kb = 0; kb < nkb && ok && !(WGRAD_SP_EXP & 8); ++kb) {
+      for (int kb = 0; kb < nkb && ok; ++kb) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
+          if (ew == 0 && h == 0) WGRAD_TRACE_EV(kTrEpiWaitStart, trace_b);
           WGRAD_PROF_T(te0);
           ok = mbar_wait(&tfull_bar[h], aphase, abort_flag, kDevTimeoutEpilogue);
           WGRAD_PROF_ADD(kProfEpiWait, te0);
           WGRAD_PROF_T(te1);
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) continue;
+          if (ew == 0 && h == 0) WGRAD_TRACE_EV(kTrEpiReady, trace_b);
           tc_fence_after();
           const uint32_t t_p = tmem_base + lane_addr + static_cast<uint32_t>(h * 2 * C::HALF + cg * C::G);
-          // Two 32-column chunks of P and S each; the slot goes back to the MMA
-          // thread as soon as the second chunk is in registers.
+          // SP_CHUNK-column pieces of P and S; the slot goes back to the MMA
+          // thread as soon as the last piece is in registers.
           uint32_t rp[SP_CHUNK], rs[SP_CHUNK];
 #pragma unroll
           for (int c = 0; c < C::G / SP_CHUNK; ++c) {
-            if (!(WGRAD_SP_EXP & 2)) tmem_ld_chunk(t_p + c * SP_CHUNK, rp);
-            if (!(WGRAD_SP_EXP & 3)) tmem_ld_chunk(t_p + C::HALF + c * SP_CHUNK, rs);
+            tmem_ld_chunk(t_p + c * SP_CHUNK, rp);
+            tmem_ld_chunk(t_p + C::HALF + c * SP_CHUNK, rs);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < SP_CHUNK; ++i) asm volatile("" : "+r"(rp[i]), "+r"(rs[i]));
@@ -373,6 +345,7 @@ __global__ void __launch_bounds__(SpCfg<EPI>::THREADS, 1)
                 if (rank != 0) mbar_arrive_cluster(tempty_leader0 + static_cast<uint32_t>(h * sizeof(uint64_t)));
                 else mbar_arrive(&tempty_bar[h]);
               }
+              if (ew == 0) WGRAD_TRACE_EV(h == 0 ? kTrEpiReleased : kTrEpiDone, trace_b);
             }
             float* f = &fin[h * C::G + c * SP_CHUNK];
 #pragma unroll
@@ -384,13 +357,8 @@ __global__ void __launch_bounds__(SpCfg<EPI>::THREADS, 1)
               const float s1 = unit_scales ? 1.f : __uint_as_float(rs[j + 1]);
               fma_f32x2(f[j], f[j + 1], p0, p1, s0, s1, f[j], f[j + 1]);
 #else
-              if (WGRAD_SP_FMA2) {
-                fma_f32x2(f[j], f[j + 1], __uint_as_float(rp[j]), __uint_as_float(rp[j + 1]), __uint_as_float(rs[j]),
-                          __uint_as_float(rs[j + 1]), f[j], f[j + 1]);
-              } else {
-                f[j] = __fmaf_rn(__uint_as_float(rp[j]), __uint_as_float(rs[j]), f[j]);
-                f[j + 1] = __fmaf_rn(__uint_as_float(rp[j + 1]), __uint_as_float(rs[j + 1]), f[j + 1]);
-              }
+              fma_f32x2(f[j], f[j + 1], __uint_as_float(rp[j]), __uint_as_float(rp[j + 1]), __uint_as_float(rs[j]),
+                        __uint_as_float(rs[j + 1]), f[j], f[j + 1]);
 #endif
             }
           }
@@ -398,6 +366,7 @@ __global__ void __launch_bounds__(SpCfg<EPI>::THREADS, 1)
         }
         WGRAD_PROF_INC(kProfKBlocks);
         aphase ^= 1u;
+        ++trace_b;
       }
       if (!ok) break;
 
@@ -433,7 +402,10 @@ __global__ void __launch_bounds__(SpCfg<EPI>::THREADS, 1)
   __syncthreads();
   cluster_sync();  // no cross-CTA arrival or UMMA is left in flight
 #if WGRAD_PROFILE
-  if (threadIdx.x < kProfSlots) atomicAdd(&g_wgrad_prof[threadIdx.x], s_prof[threadIdx.x]);
+  if (threadIdx.x < kProfSlots)
+    atomicAdd(&g_wgrad_prof[threadIdx.x], threadIdx.x == kProfCtaCycles
+                                              ? static_cast<unsigned long long>(clock64() - t_cta0)
+                                              : s_prof[threadIdx.x]);
 #endif
   if (warp == 1) {
     tc_fence_after();

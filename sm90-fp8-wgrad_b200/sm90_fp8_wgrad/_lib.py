@@ -199,7 +199,7 @@ def check(status: int, what: str) -> None:
 
 PROFILE_SLOTS = ("producer_wait_stage", "producer_wait_scales", "mma_wait", "mma_issue", "epi_wait",
                  "epi_promote", "epi_store", "epi_store_wait", "k_blocks", "tiles", "ctas", "sf_convert",
-                 "sf_publish", "load_latency", "sf_sync", "sf_load", "mma_tile_wait")
+                 "sf_publish", "load_latency", "sf_sync", "sf_load", "mma_tile_wait", "cta_cycles")
 
 
 def profile_counters() -> dict[str, int] | None:

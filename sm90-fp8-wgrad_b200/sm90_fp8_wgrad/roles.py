@@ -58,6 +58,8 @@ def main(argv: list[str] | None = None) -> int:
                      if key not in ("k_blocks", "tiles", "ctas") and (v or not key.startswith(("sf_", "mma_tile")))}
         # load_latency is summed by the MMA warp over every K block it waited for
         per_block["load_latency"] = round(c.get("load_latency", 0) / max(c["k_blocks"], 1))
+        # the CTA's whole run (set-up excluded) per K block: the period every role shares
+        per_block["period"] = round(c.get("cta_cycles", 0) / blocks)
         print(json.dumps({"workload": a.workload, "gemm": name, "ctas": c["ctas"],
                           "k_blocks_per_cta": round(c["k_blocks"] / max(c["ctas"], 1)),
                           "tiles_per_cta": round(c["tiles"] / max(c["ctas"], 1)),

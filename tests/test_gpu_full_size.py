@@ -146,3 +146,71 @@ def test_full_size_accumulate_and_expert_ranges(cuda_device):
         k0, k1, b0 = cu[e], cu[e + 1], bo[e]
         ref = _dequant(lhs, k0, k1, b0).t() @ _dequant(rhs, k0, k1, b0)
         assert _calc_diff(base[e], ref) <= 1e-5
+
+
+@pytest.mark.parametrize("name", ["dsv3_32k", "dsv3_skewed_32k"])
+def test_full_size_every_expert(cuda_device, name):
+    """Whole-output correctness at full size, as the reference's benchmark
+    checks it (scripts/benchmark_wgrad.py:360-414): every expert of both GEMMs
+    against an fp32 dequantise-then-matmul of the same FP8 operands, DeepSeek
+    calc_diff accumulated over the whole output of each GEMM (vs the reference
+    rounded to BF16, the reference's metric, and vs the fp32 reference) within
+    1e-5; every output finite, every empty expert zero."""
+    from sm90_fp8_wgrad.matrix import check_all_experts
+    from sm90_fp8_wgrad.routing import make_routing
+    from sm90_fp8_wgrad.synthetic import make_synthetic_wgrad_inputs, run_custom_down, run_custom_gate_up
+
+    experts, top_k, hidden, inter, tokens, route, _ = CONFIGS[name]
+    routing = make_routing(tokens=tokens, experts=experts, top_k=top_k, route=route, seed=1234)
+    inp = make_synthetic_wgrad_inputs(tokens=tokens, experts=experts, top_k=top_k, hidden=hidden,
+                                      intermediate=inter, route=route, seed=1234, device=cuda_device,
+                                      routing=routing)
+    inp.drop_sources()
+    run_custom_down(inp)
+    run_custom_gate_up(inp)
+    torch.cuda.synchronize()
+    r = check_all_experts(inp, "padded")
+    assert r["experts_checked"] == sum(1 for c in inp.counts if c > 0), r
+    assert r["finite"] and r["empty_experts_zero"], r
+    assert r["calc_diff_max"] <= 1e-5 and r["calc_diff_vs_fp32_max"] <= 1e-5, r
+
+
+def test_full_size_quantiser_sampled_blocks_bit_exact(cuda_device):
+    """The CUDA quantiser's bytes and scales at DeepSeek-V3 32k size, on sampled
+    (scale block, 64-column strip) pieces of all four operands, bit for bit
+    against the oracle's restatement of the reference quantiser
+    (quant.py:129-167) applied to the same BF16 rows."""
+    import numpy as np
+
+    import wgrad_oracle as O
+    from sm90_fp8_wgrad.routing import make_routing
+    from sm90_fp8_wgrad.synthetic import make_synthetic_wgrad_inputs
+
+    experts, top_k, hidden, inter, tokens, route, _ = CONFIGS["dsv3_32k"]
+    routing = make_routing(tokens=tokens, experts=experts, top_k=top_k, route=route, seed=1234)
+    inp = make_synthetic_wgrad_inputs(tokens=tokens, experts=experts, top_k=top_k, hidden=hidden,
+                                      intermediate=inter, route=route, seed=1234, device=cuda_device,
+                                      routing=routing, allocate_custom_outputs=False)
+    torch.cuda.synchronize()
+    rs = inp.meta.block_row_start.cpu().numpy()
+    rc = inp.meta.block_row_count.cpu().numpy()
+    rng = random.Random(11)
+    pairs = ((inp.grad_y_grouped_bf16, inp.grad_y_q), (inp.hidden_grouped_bf16, inp.hidden_q),
+             (inp.grad_gate_up_grouped_bf16, inp.grad_gate_up_q), (inp.x_grouped_bf16, inp.x_q))
+    checked = 0
+    for src, op in pairs:
+        cols = src.shape[1]
+        pitch = op.data.stride(1)
+        storage = op.data.as_strided((cols, pitch), (pitch, 1))
+        for _ in range(12):
+            b = rng.randrange(int(inp.meta.total_blocks))
+            c0 = rng.randrange(cols // 64) * 64
+            r0, n = int(rs[b]), int(rc[b])
+            x = src[r0:r0 + n, c0:c0 + 64].float().cpu().numpy()
+            ref = O.quantize_blocks(x, [0], [n], 128, 128)
+            got = storage[c0:c0 + 64, b * 128:(b + 1) * 128].view(torch.uint8).cpu().numpy()
+            np.testing.assert_array_equal(got, ref.data[:, :128], err_msg=f"block {b} cols {c0}")
+            np.testing.assert_array_equal(op.scales[b, c0:c0 + 64].cpu().numpy().view(np.uint32),
+                                          ref.scales[0].view(np.uint32), err_msg=f"scales block {b} cols {c0}")
+            checked += 1
+    assert checked == 48
