@@ -17,6 +17,19 @@ It imports the reference package ``sm90_fp8_wgrad`` (pure Python) and records:
                         transliterated here in PyTorch (masked amax, fp32
                         ``amax / 448`` floored at 1e-12, ``x / scale``,
                         ``tensor.to(torch.float8_e4m3fn)``).
+* quant_triton.npz   -- the reference's own quantiser, end to end: its launcher
+                        quantize_grouped_wgrad_operand_128x1 (quant.py:175-270)
+                        and Triton kernel (quant.py:105-167), run on CPU under
+                        the Triton interpreter (TRITON_INTERPRET=1, set before
+                        triton is imported), padded and packed layouts. The
+                        interpreter converts fp32 to e4m3 in software and
+                        differs from the GPU's round-to-nearest-even satfinite
+                        conversion in two ways: a quotient exactly halfway
+                        between two e4m3 values goes to the larger magnitude,
+                        and a round-up that should carry into the next binade
+                        does not. The fixture stores the interpreter's bytes;
+                        the test explains every byte that differs from the
+                        oracle by one of those two rules.
 * wgrad_small.npz    -- ref_scaled_wgrad (checks.py:42-61) fp32 outputs and the
                         reference calc_diff (checks.py:175-187) of known pairs.
 * c1_tiny.npz        -- the tiny benchmark configuration (E=8, top-2, H=256,
@@ -31,8 +44,13 @@ from __future__ import annotations
 
 import argparse
 import hashlib
+import os
 import sys
 from pathlib import Path
+
+# The reference's Triton quantiser runs on CPU through the Triton interpreter;
+# the switch must be set before anything imports triton.
+os.environ.setdefault("TRITON_INTERPRET", "1")
 
 import numpy as np
 import torch
@@ -86,6 +104,19 @@ def torch_quantize_like_triton(x_bf16: torch.Tensor, meta) -> tuple[np.ndarray, 
         q = (vals / scale[None, :]).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
         data[:, b * 128 : b * 128 + rows] = q[:rows].T
     return data, scales
+
+
+def reference_triton_quantize(x_bf16: torch.Tensor, meta, ref_quant, layout: str) -> dict:
+    """The reference launcher + Triton kernel under the interpreter, on CPU.
+    Returns the operand storage bytes ([cols][pitch]), the packed launch copy
+    ([cols][K], packed layout only) and the scales."""
+    op = ref_quant.quantize_grouped_wgrad_operand_128x1(x_bf16.as_subclass(_CudaLike), meta, layout_mode=layout)
+    data = op.data.as_subclass(torch.Tensor)             # logical [K, cols], K contiguous
+    out = {"storage": data.t().contiguous().view(torch.uint8).numpy().copy(),   # [cols][K]
+           "scales": op.scales.as_subclass(torch.Tensor).numpy().copy()}
+    if op.kernel_data is not None:
+        out["kernel_data"] = op.kernel_data.as_subclass(torch.Tensor).view(torch.uint8).numpy().copy()
+    return out
 
 
 def _operand(data: np.ndarray, scales: np.ndarray, k_rows: int, ref_quant):
@@ -154,6 +185,20 @@ def main() -> None:
             max_abs, max_rel, max_ref = ref_checks.scaled_wgrad_error(ref.to(torch.bfloat16), ref)
             w_out[f"{name}.{stage}.error_bf16_vs_f32"] = np.asarray([max_abs, max_rel, max_ref], np.float64)
     np.savez_compressed(HERE / "quant_small.npz", **q_out)
+
+    # ------------------- the reference's Triton quantiser itself (interpreter)
+    t_out = {"generator": np.asarray("reference quantize_grouped_wgrad_operand_128x1 + Triton kernel, "
+                                     "TRITON_INTERPRET=1 on CPU")}
+    for name, spec in SMALL_CASES.items():
+        inp = case_inputs(spec)
+        meta = ref_meta.build_wgrad_scale_block_meta(cu_of(spec["counts"]))
+        for key in ("lhs_down", "rhs_down", "lhs_gate", "rhs_gate"):
+            x = torch.from_numpy(bf16_from_f32(inp[key])).view(torch.bfloat16)
+            for layout in ("padded", "packed"):
+                r = reference_triton_quantize(x, meta, ref_quant, layout)
+                for k, v in r.items():
+                    t_out[f"{name}.{key}.{layout}.{k}"] = v
+    np.savez_compressed(HERE / "quant_triton.npz", **t_out)
     np.savez_compressed(HERE / "wgrad_small.npz", **w_out)
 
     # ---------------------------------------------------------- tiny C1 config
