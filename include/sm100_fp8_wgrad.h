@@ -139,6 +139,24 @@ SM100_WGRAD_API int sm100_fp8_grouped_wgrad(const Sm100WgradArgs* args, void* st
 SM100_WGRAD_API int sm100_wgrad_workspace_bytes(const Sm100WgradArgs* args, int64_t* bytes);
 
 /*
+ * The scale-product GEMM (SM100_WGRAD_TILE_256x256_SP, or _SP_W16; AUTO means
+ * _SP) for callers that cannot allocate device memory, such as a host binding
+ * that owns only the buffers it was given, or a process that reserves all of
+ * its device memory up front. It needs no workspace: the split scales live in
+ * a 64 MiB array compiled into the library (every GPU that loads the library
+ * holds it until exit), so args->workspace is ignored and a problem whose
+ * sm100_wgrad_workspace_bytes exceeds 64 MiB is refused with
+ * SM100_WGRAD_ERR_UNSUPPORTED. All calls share that array: calls that overlap
+ * on the GPU (other streams, other threads on the same device) race, so
+ * serialise them. The first call on a device looks up the array's device
+ * address (make it before any stream capture). It allocates nothing, and
+ * device errors of its launches are read with sm100_wgrad_device_error.
+ * No counterpart in the reference: its launcher always allocates through the
+ * framework.
+ */
+SM100_WGRAD_API int sm100_fp8_grouped_wgrad_noalloc(const Sm100WgradArgs* args, void* stream);
+
+/*
  * 1x128 FP8 quantiser: per (128-row block b, column c)
  *   amax = max_{k < row_count[b]} |x[row_start[b] + k, c]|
  *   scale[b, c] = max(amax / 448, 1e-12)

@@ -6,3 +6,4 @@
 #include "quant.cu"
 #include "meta.cu"
 #include "capi.cu"
+#include "noalloc.cu"

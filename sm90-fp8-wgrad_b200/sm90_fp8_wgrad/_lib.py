@@ -45,6 +45,7 @@ SCALE_UE8M0 = 1
 # Every symbol include/sm100_fp8_wgrad.h declares.
 EXPORTED_SYMBOLS = (
     "sm100_fp8_grouped_wgrad",
+    "sm100_fp8_grouped_wgrad_noalloc",
     "sm100_wgrad_workspace_bytes",
     "sm100_wgrad_quantize_1x128",
     "sm100_wgrad_quantize_1x128_ex",
@@ -157,6 +158,8 @@ def load() -> ctypes.CDLL:
             raise RuntimeError(f"cannot load {path}: {exc}") from exc
         lib.sm100_fp8_grouped_wgrad.argtypes = [ctypes.POINTER(Sm100WgradArgs), ctypes.c_void_p]
         lib.sm100_fp8_grouped_wgrad.restype = ctypes.c_int
+        lib.sm100_fp8_grouped_wgrad_noalloc.argtypes = [ctypes.POINTER(Sm100WgradArgs), ctypes.c_void_p]
+        lib.sm100_fp8_grouped_wgrad_noalloc.restype = ctypes.c_int
         lib.sm100_wgrad_workspace_bytes.argtypes = [ctypes.POINTER(Sm100WgradArgs), ctypes.POINTER(ctypes.c_int64)]
         lib.sm100_wgrad_workspace_bytes.restype = ctypes.c_int
         lib.sm100_wgrad_quantize_1x128.argtypes = [
