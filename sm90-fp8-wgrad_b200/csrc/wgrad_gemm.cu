@@ -171,6 +171,17 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
+// Tile a persistent CTA (or CTA pair) `begin` of `stride` takes in round r.
+// CTA pairs walk the (LPT expert, m, n) list alternately forward and
+// backward (boustrophedon), so over two rounds every pair gets one tile from
+// the costlier and one from the cheaper end of each stretch of the sorted
+// list (measured 1-3 % faster for pairs; neutral to slightly slower for the
+// single-CTA tiles, which keep the plain round robin).
+template <bool SNAKE>
+__device__ __forceinline__ int sched_tile(int r, int begin, int stride) {
+  return SNAKE ? r * stride + ((r & 1) ? stride - 1 - begin : begin) : r * stride + begin;
+}
+
 struct TileCoord {
   int e, m0, n0;
 };
@@ -215,7 +226,8 @@ __device__ __forceinline__ void run_producer(const CUtensorMap& tmap_a, const CU
   int stage = 0, sstage = 0;
   uint32_t phase = 0, sphase = 0;
   bool ok = true;
-  for (int tile = tile_begin; tile < p.num_tiles && ok; tile += tile_stride) {
+  for (int r = 0, tile = tile_begin; r * tile_stride < p.num_tiles && ok; tile = sched_tile<PAIR>(++r, tile_begin, tile_stride)) {
+    if (tile >= p.num_tiles) continue;
     const TileCoord tc = decode_tile(p, tile, static_cast<int>(rank) * BM);
     const int kb0 = __ldg(p.block_offsets + tc.e);
     const int nkb = __ldg(p.block_offsets + tc.e + 1) - kb0;
@@ -232,7 +244,7 @@ __device__ __forceinline__ void run_producer(const CUtensorMap& tmap_a, const CU
       // Test-only failure injection: announce the first stage's bytes but
       // issue no copy, so the stage never fills and the bounded waits of
       // the consumers expire (device error word, clean exit).
-      const bool withhold = p.inject == kInjectWithholdFirstLoad && tile == tile_begin && kb == 0;
+      const bool withhold = p.inject == kInjectWithholdFirstLoad && r == 0 && kb == 0;
       if constexpr (PAIR) {
         const uint32_t leader_full = cluster_addr(&full_bar[stage], 0);
         if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * (C::A_BYTES + C::B_BYTES));
@@ -521,7 +533,8 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
     int stage = 0, acc = 0;
     uint32_t phase = 0, aphase = 0;
     bool ok = true;
-    for (int tile = tile_begin; tile < p.num_tiles && ok; tile += tile_stride) {
+    for (int r = 0, tile = tile_begin; r * tile_stride < p.num_tiles && ok; tile = sched_tile<PAIR>(++r, tile_begin, tile_stride)) {
+    if (tile >= p.num_tiles) continue;
       const TileCoord tc = decode_tile(p, tile);
       const int nkb = __ldg(p.block_offsets + tc.e + 1) - __ldg(p.block_offsets + tc.e);
       // K slices of 32 rows in the expert's last block: 4 in the padded layout;
@@ -595,7 +608,8 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
     // the partial's release goes to the pair's even CTA
     const uint32_t tempty_addr0 = PAIR ? cluster_addr(&tempty_bar[0], 0) : 0u;
     int trace_b = 0;
-    for (int tile = tile_begin; tile < p.num_tiles && ok; tile += tile_stride) {
+    for (int r = 0, tile = tile_begin; r * tile_stride < p.num_tiles && ok; tile = sched_tile<PAIR>(++r, tile_begin, tile_stride)) {
+    if (tile >= p.num_tiles) continue;
       const TileCoord tc = decode_tile(p, tile, row_off);
       const int nkb = __ldg(p.block_offsets + tc.e + 1) - __ldg(p.block_offsets + tc.e);
       float fin[C::COLS_PER_WARP];
