@@ -6,7 +6,10 @@ Output: sm90-fp8-wgrad_b200/sm90_fp8_wgrad/_lib/libsm100_fp8_wgrad.so
         counters, -DWGRAD_PROFILE=1, read with sm90_fp8_wgrad._lib.profile_counters();
         --debug-modes: libsm100_fp8_wgrad_debug.so with the known-answer kernel
         modes of KERNEL_LAB_WGRAD_KERNEL_MODE, -DWGRAD_DEBUG_MODES=1. Load either
-        with SM100_WGRAD_LIB=<path>.)
+        with SM100_WGRAD_LIB=<path>.
+        --trace N: libsm100_fp8_wgrad_trace.so with per-K-block clock64 event
+        stamps of CTAs 0 and 1 (-DWGRAD_TRACE=N: 1 MMA issuer + promotion warp,
+        2 per-chunk promotion stamps), printed by python -m sm90_fp8_wgrad.timeline.)
 """
 from __future__ import annotations
 
@@ -22,6 +25,7 @@ CSRC = HERE / "csrc"
 OUT = HERE / "sm90_fp8_wgrad" / "_lib" / "libsm100_fp8_wgrad.so"
 OUT_PROFILE = HERE / "sm90_fp8_wgrad" / "_lib" / "libsm100_fp8_wgrad_profile.so"
 OUT_DEBUG = HERE / "sm90_fp8_wgrad" / "_lib" / "libsm100_fp8_wgrad_debug.so"
+OUT_TRACE = HERE / "sm90_fp8_wgrad" / "_lib" / "libsm100_fp8_wgrad_trace{}.so"
 SOURCES = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [HERE.parent / "include" / "sm100_fp8_wgrad.h"]
 
 
@@ -39,8 +43,9 @@ def needs_build(out: Path = OUT) -> bool:
     return any(s.stat().st_mtime > mtime for s in SOURCES)
 
 
-def build(force: bool = False, verbose: bool = False, profile: bool = False, debug_modes: bool = False) -> Path:
-    out = OUT_DEBUG if debug_modes else (OUT_PROFILE if profile else OUT)
+def build(force: bool = False, verbose: bool = False, profile: bool = False, debug_modes: bool = False,
+          trace: int = 0) -> Path:
+    out = Path(str(OUT_TRACE).format(trace)) if trace else (OUT_DEBUG if debug_modes else (OUT_PROFILE if profile else OUT))
     if not force and not needs_build(out):
         return out
     out.parent.mkdir(parents=True, exist_ok=True)
@@ -50,6 +55,7 @@ def build(force: bool = False, verbose: bool = False, profile: bool = False, deb
         "-shared", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-Xptxas", "-v" if verbose else "-O3",
         *(["-DWGRAD_PROFILE=1"] if profile else []),
         *(["-DWGRAD_DEBUG_MODES=1"] if debug_modes else []),
+        *([f"-DWGRAD_TRACE={int(trace)}"] if trace else []),
         "-o", str(tmp), str(CSRC / "unity.cu"),
     ]
     res = subprocess.run(cmd, capture_output=True, text=True)
@@ -67,5 +73,6 @@ if __name__ == "__main__":
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--profile", action="store_true", help="build the per-role cycle-counter library")
     ap.add_argument("--debug-modes", action="store_true", help="build the known-answer kernel-mode library")
+    ap.add_argument("--trace", type=int, choices=(1, 2), default=0, help="build the event-trace library")
     a = ap.parse_args()
-    print(build(force=a.force, verbose=a.verbose, profile=a.profile, debug_modes=a.debug_modes))
+    print(build(force=a.force, verbose=a.verbose, profile=a.profile, debug_modes=a.debug_modes, trace=a.trace))
