@@ -285,7 +285,7 @@ SM100_WGRAD_API int sm100_wgrad_build_flags(void);
  * stage latency (TMA issue to the MMA warp seeing the stage full); 14-15: UE8M0
  * writer vote and scale loads; 16: UE8M0 MMA wait for a free accumulator. The
  * UE8M0 kernel records its scale-factor writer in slots 4-5 and its epilogue's
- * accumulator wait in slot 7. */
+ * accumulator wait in slot 7. 17: cycles from a CTA's start to its exit. */
 SM100_WGRAD_API int sm100_wgrad_profile_counters(uint64_t* counters, int32_t n);
 
 /* Human-readable text of a status code (static storage). */
