@@ -394,6 +394,54 @@ def _tensor_rate_tflops(dev, sm_mhz: float) -> float:
     return sms * 8192 * 2 * sm_mhz * 1e6 / 1e12
 
 
+def library_fp8_rate(dev, gpu_index: int, seconds: float = 3.0) -> dict:
+    """cuBLAS FP8 GEMM on the same GPU, for context beside the grouped Wgrad rate.
+
+    ``torch._scaled_mm`` on 8192^3 e4m3 operands with one scale per tensor (no
+    per-block promotion; cuBLAS offers 1x128 block scaling only on sm_90):
+    best of 10 launches (burst) and back-to-back launches for ``seconds``
+    (sustained, under the board power limit), with the SM clock seen meanwhile.
+    """
+    n = 8192
+    a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn).t()
+    one = torch.ones((), device=dev)
+    flops = 2.0 * n ** 3
+
+    def gemm():
+        return torch._scaled_mm(a, b, one, one, out_dtype=torch.bfloat16)
+
+    for _ in range(3):
+        gemm()
+    torch.cuda.synchronize(dev)
+    best = float("inf")
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        gemm()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        best = min(best, e0.elapsed_time(e1))
+    clocks = ClockSampler(dev, gpu_index)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    t0 = time.perf_counter()
+    e0.record()
+    while time.perf_counter() - t0 < seconds:
+        for _ in range(20):
+            gemm()
+        launches += 20
+        torch.cuda.synchronize(dev)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    return {"what": "cuBLAS FP8 e4m3 GEMM 8192^3, per-tensor scales (torch._scaled_mm), bf16 out",
+            "burst_tflops": flops / (best * 1e-3) / 1e12,
+            "sustained_tflops": flops * launches / (e0.elapsed_time(e1) * 1e-3) / 1e12,
+            "sustained_seconds": seconds, "sustained_clocks": clk}
+
+
 def run_ours(args) -> None:
     rank, world, local_rank = dist_env()
     dev = torch.device("cuda", local_rank)
@@ -494,6 +542,11 @@ def run_ours(args) -> None:
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(inp, args, world, dev, f_down + f_gate)
+    lib_rate = None
+    if rank == 0 and world == 1 and not args.no_library_rate:
+        lib_rate = library_fp8_rate(dev, clocks.gpu_index)
+        lib_rate["pct_burst"] = value / lib_rate["burst_tflops"]
+        lib_rate["pct_sustained"] = value / lib_rate["sustained_tflops"]
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(_host_threads())   # after the GPU timing: all host cores for the CPU leg
@@ -530,6 +583,9 @@ def run_ours(args) -> None:
                                             if clk and clk.get("sm_mhz") else None),
             "tflops_per_gpu_per_ghz": (value / world / (clk["sm_mhz"] / 1000.0) if clk and clk.get("sm_mhz") else None),
             "hbm_gbs_step": step_bytes / (local_ms * 1e-3) / 1e9,
+            # This run's grouped Wgrad rate as a fraction of a plain cuBLAS FP8 GEMM's
+            # (no promotion) on the same GPU, burst and sustained at the power limit.
+            "library_fp8": lib_rate,
             "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": e2e,
@@ -661,6 +717,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-library-rate", action="store_true",
+                    help="skip the cuBLAS FP8 GEMM rate measured after the timed region (about 5 s)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         log("warm-up raised to 3 (timing rule)")
