@@ -380,6 +380,19 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 
+// 16 lanes x 256 bits per repetition (.x4: four 8-column groups): thread t of
+// the warp receives, for group g, lane (taddr.lane + t / 4) at columns
+// 8 g + 2 (t % 4) and + 1 in registers 4 g and 4 g + 1, and lane
+// (taddr.lane + 8 + t / 4) at the same columns in registers 4 g + 2 and 4 g + 3.
+__device__ __forceinline__ void tmem_ld_16x256b_x4(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 // Shared memory -> TMEM copy of a 32-row x 128-bit matrix, replicated into all
 // four lane quarters (tcgen05.cp 32x128b.warpx4): row r lands in lane
 // 32 q + r of every quarter q, its 16 bytes in columns [taddr.col, +4).

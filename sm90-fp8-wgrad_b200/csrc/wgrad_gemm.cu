@@ -119,6 +119,10 @@ constexpr int FIRST_EPI_WARP = 4;
 // promotion warps take the rest: 16 warps: 640 x 96 = 128 x 32 + 512 x 112;
 // 8 warps: 384 x 168 >= 128 x 56 + 256 x 224; 4 warps, 2 CTAs: 256 x 128 =
 // 128 x 56 + 128 x 200.
+#ifndef WGRAD_FRAG16
+#define WGRAD_FRAG16 1
+#endif
+
 template <int BN, int EPI, bool PAIR = false>
 struct Cfg {
   static constexpr int EPI_WARPS = EPI;
@@ -137,6 +141,11 @@ struct Cfg {
   static constexpr int COLS_PER_WARP = BN / (EPI_WARPS / 4);  // EPI_WARPS / 4 column groups
   // tcgen05.ld columns per load: 32 when two such buffers fit beside the accumulator
   static constexpr int CHUNK = REGS_EPILOGUE >= COLS_PER_WARP + 80 ? 32 : 16;
+  // Promotion in the 16x256b fragment layout (two rows and a column pair per
+  // thread): 8-byte column-scale loads shared by 8 lanes' rows instead of a
+  // 16-byte broadcast per 4 columns, a quarter of the shared-memory wavefronts.
+  static constexpr bool FRAG16 = WGRAD_FRAG16 != 0 && EPI_WARPS == 8 && BN == 256;
+  static constexpr int GC = CHUNK / 8;  // 8-column groups per chunk of the fragment layout
   static constexpr int CHUNKS = COLS_PER_WARP / CHUNK;
   static constexpr int OUT_STAGE_BYTES_PER_WARP =
       COLS_PER_WARP * 32 * 2 >= 8192 ? 8192 : 4096;
@@ -293,6 +302,38 @@ __device__ __forceinline__ void run_producer(const CUtensorMap& tmap_a, const CU
 // match); fp32 boxes are 32 columns (128B swizzle). The caller has waited for
 // the warp's previous store to finish reading the staging area. Returns
 // false when a wait gave up.
+// accumulate: the previous output boxes come in through the same tensor map
+// and swizzled staging layout the store uses (TMA load into this warp's
+// staging area, bounded wait), so each thread adds its own elements.
+// Box b of the round covers output columns [col_of(b), +box width).
+template <class ColOf>
+__device__ __forceinline__ bool load_previous_boxes(const CUtensorMap& tmap_out, const GemmParams& p,
+                                                    const TileCoord& tc, int quarter, int lane, uint8_t* stage_out,
+                                                    uint64_t* oldout_bar, uint32_t& oldout_phase,
+                                                    volatile int* abort_flag, int nboxes, int box_bytes,
+                                                    ColOf col_of) {
+  if (lane == 0) {
+    uint32_t bytes = 0;
+    for (int b = 0; b < nboxes; ++b) bytes += col_of(b) < p.n ? box_bytes : 0u;
+    mbar_arrive_expect_tx(oldout_bar, bytes);
+    for (int b = 0; b < nboxes; ++b) {
+      const int c = col_of(b);
+      if (c < p.n) tma_load_3d(stage_out + b * box_bytes, &tmap_out, oldout_bar, c, tc.m0 + quarter * 32, tc.e);
+    }
+  }
+  const bool landed = mbar_wait(oldout_bar, oldout_phase, abort_flag, kDevTimeoutEpilogue);
+  if (!landed) {
+    // Giving up (timeout, or another role aborted): let this warp's own
+    // load land before the CTA exits. Bounded, regardless of the abort flag.
+    const uint32_t addr = smem_u32(oldout_bar);
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(addr, oldout_phase) && globaltimer_ns() - t0 < WGRAD_WAIT_TIMEOUT_NS) {
+    }
+  }
+  oldout_phase ^= 1u;
+  return __all_sync(0xffffffffu, landed);
+}
+
 template <int COLS, int OUT_STAGE_BYTES, int GSTRIDE = 64, int GCOLS = 64, int BOXC = 64>
 __device__ __forceinline__ bool store_warp_tile(float (&fin)[COLS], const CUtensorMap& tmap_out, const GemmParams& p,
                                                 const TileCoord& tc, int quarter, int lane, int col0,
@@ -305,30 +346,9 @@ __device__ __forceinline__ bool store_warp_tile(float (&fin)[COLS], const CUtens
   const bool rows_in = (tc.m0 + quarter * 32) < p.m;
   const uint32_t swz = static_cast<uint32_t>(lane & 7);
   auto colof = [&](int f) -> int { return col0 + (f / GCOLS) * GSTRIDE + (f % GCOLS); };
-  // accumulate: the previous output boxes come in through the same tensor
-  // map and swizzled staging layout the store uses (TMA load into this
-  // warp's staging area, bounded wait), so each thread adds its own row.
   auto load_previous = [&](int nboxes, int box_cols, int box_bytes, int first_box) -> bool {
-    if (lane == 0) {
-      uint32_t bytes = 0;
-      for (int b = 0; b < nboxes; ++b) bytes += colof((first_box + b) * box_cols) < p.n ? box_bytes : 0u;
-      mbar_arrive_expect_tx(oldout_bar, bytes);
-      for (int b = 0; b < nboxes; ++b) {
-        const int c = colof((first_box + b) * box_cols);
-        if (c < p.n) tma_load_3d(stage_out + b * box_bytes, &tmap_out, oldout_bar, c, tc.m0 + quarter * 32, tc.e);
-      }
-    }
-    const bool landed = mbar_wait(oldout_bar, oldout_phase, abort_flag, kDevTimeoutEpilogue);
-    if (!landed) {
-      // Giving up (timeout, or another role aborted): let this warp's own
-      // load land before the CTA exits. Bounded, regardless of the abort flag.
-      const uint32_t addr = smem_u32(oldout_bar);
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(addr, oldout_phase) && globaltimer_ns() - t0 < WGRAD_WAIT_TIMEOUT_NS) {
-      }
-    }
-    oldout_phase ^= 1u;
-    return __all_sync(0xffffffffu, landed);
+    return load_previous_boxes(tmap_out, p, tc, quarter, lane, stage_out, oldout_bar, oldout_phase, abort_flag,
+                               nboxes, box_bytes, [&](int b) { return colof((first_box + b) * box_cols); });
   };
   if (!p.out_f32) {
     // bf16: boxes of 32 rows x BOXC columns, BOX_BYTES each, PER_ROUND boxes
@@ -437,6 +457,143 @@ __device__ __forceinline__ bool store_warp_tile(float (&fin)[COLS], const CUtens
     }
   }
   return ok;
+}
+
+// Accumulator element f of a promotion warp in the 16x256b fragment layout
+// (see tmem_ld_16x256b_x4): chunks of GC 8-column groups, each chunk holding
+// the warp's upper 16 rows then its lower 16, four registers per group.
+// Row within the warp's 32 rows and column within its COLS columns.
+template <int GC>
+__device__ __forceinline__ int frag_row(int f, int lane) {
+  return 16 * ((f % (8 * GC)) / (4 * GC)) + 8 * ((f % 4) >> 1) + (lane >> 2);
+}
+template <int GC>
+__device__ __forceinline__ int frag_col(int f, int lane) {
+  return 8 * ((f / (8 * GC)) * GC + (f % (4 * GC)) / 4) + 2 * (lane & 3) + (f & 1);
+}
+
+__device__ __forceinline__ uint32_t ld_shared_b32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_shared_b32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint2 ld_shared_v2(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+
+// store_warp_tile for an accumulator in the fragment layout: the same boxes,
+// staging swizzle and TMA stores, each thread writing its column pairs
+// (4 bytes of bf16 or 8 bytes of fp32) into the rows it holds. Within one
+// store instruction the warp covers 8 consecutive rows at 8 different
+// swizzled 16-byte positions, so the 32 lanes hit 32 different banks.
+template <int COLS, int OUT_STAGE_BYTES, int GC>
+__device__ __forceinline__ bool store_warp_tile_frag(float (&fin)[COLS], const CUtensorMap& tmap_out,
+                                                     const GemmParams& p, const TileCoord& tc, int quarter, int lane,
+                                                     int col0, uint8_t* stage_out, uint64_t* oldout_bar,
+                                                     uint32_t& oldout_phase, volatile int* abort_flag) {
+  const uint32_t stage_addr = smem_u32(stage_out);
+  const bool rows_in = (tc.m0 + quarter * 32) < p.m;
+  const uint32_t rsw = static_cast<uint32_t>((lane >> 2) & 7);  // every row this thread holds is == lane / 4 mod 8
+  constexpr int BOXC = 64;  // bf16 box: 32 rows x 64 columns, 128-byte rows (128B swizzle)
+  if (!p.out_f32) {
+    constexpr int BOX_BYTES = 32 * BOXC * 2;
+    constexpr int BOXES = COLS / BOXC;
+    constexpr int PER_ROUND = OUT_STAGE_BYTES / BOX_BYTES < BOXES ? OUT_STAGE_BYTES / BOX_BYTES : BOXES;
+#pragma unroll
+    for (int bx0 = 0; bx0 < BOXES; bx0 += PER_ROUND) {
+      if (bx0 > 0) {
+        if (lane == 0) bulk_wait_group_read0();
+        __syncwarp();
+      }
+      auto addr_of = [&](int f) -> uint32_t {
+        const int c = frag_col<GC>(f, lane);
+        const int r = frag_row<GC>(f, lane);
+        return stage_addr + (c / BOXC - bx0) * BOX_BYTES + r * (BOXC * 2) +
+               ((static_cast<uint32_t>((c % BOXC) >> 3) ^ rsw) << 4) + 2 * (c & 7);
+      };
+      if (p.accumulate && rows_in) {
+        if (!load_previous_boxes(tmap_out, p, tc, quarter, lane, stage_out, oldout_bar, oldout_phase, abort_flag,
+                                 PER_ROUND, BOX_BYTES, [&](int b) { return col0 + (bx0 + b) * BOXC; }))
+          return false;
+#pragma unroll
+        for (int f = 0; f < COLS; f += 2) {
+          if (frag_col<GC>(f, 0) / BOXC < bx0 || frag_col<GC>(f, 0) / BOXC >= bx0 + PER_ROUND) continue;
+          const uint32_t w = ld_shared_b32(addr_of(f));
+          const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+          fin[f] += v.x;
+          fin[f + 1] += v.y;
+        }
+      }
+#pragma unroll
+      for (int f = 0; f < COLS; f += 2) {
+        if (frag_col<GC>(f, 0) / BOXC < bx0 || frag_col<GC>(f, 0) / BOXC >= bx0 + PER_ROUND) continue;
+        st_shared_b32(addr_of(f), pack_bf16x2(fin[f], fin[f + 1]));
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && rows_in) {
+#pragma unroll
+        for (int bi = 0; bi < PER_ROUND; ++bi) {
+          const int c = col0 + (bx0 + bi) * BOXC;
+          if (c < p.n) tma_store_3d(&tmap_out, stage_out + bi * BOX_BYTES, c, tc.m0 + quarter * 32, tc.e);
+        }
+        bulk_commit_group();
+      }
+    }
+  } else {
+    // fp32: boxes of 32 rows x 32 columns (128-byte rows), PER_ROUND boxes per round.
+    constexpr int BOXES = COLS / 32;
+    constexpr int PER_ROUND = OUT_STAGE_BYTES / 4096;
+#pragma unroll
+    for (int bx0 = 0; bx0 < BOXES; bx0 += PER_ROUND) {
+      if (bx0 > 0) {
+        if (lane == 0) bulk_wait_group_read0();
+        __syncwarp();
+      }
+      auto addr_of = [&](int f) -> uint32_t {
+        const int c = frag_col<GC>(f, lane);
+        const int r = frag_row<GC>(f, lane);
+        return stage_addr + (c / 32 - bx0) * 4096 + r * 128 +
+               ((static_cast<uint32_t>((c % 32) >> 2) ^ rsw) << 4) + 4 * (c & 3);
+      };
+      if (p.accumulate && rows_in) {
+        if (!load_previous_boxes(tmap_out, p, tc, quarter, lane, stage_out, oldout_bar, oldout_phase, abort_flag,
+                                 PER_ROUND, 4096, [&](int b) { return col0 + (bx0 + b) * 32; }))
+          return false;
+#pragma unroll
+        for (int f = 0; f < COLS; f += 2) {
+          if (frag_col<GC>(f, 0) / 32 < bx0 || frag_col<GC>(f, 0) / 32 >= bx0 + PER_ROUND) continue;
+          const uint2 w = ld_shared_v2(addr_of(f));
+          fin[f] += __uint_as_float(w.x);
+          fin[f + 1] += __uint_as_float(w.y);
+        }
+      }
+#pragma unroll
+      for (int f = 0; f < COLS; f += 2) {
+        if (frag_col<GC>(f, 0) / 32 < bx0 || frag_col<GC>(f, 0) / 32 >= bx0 + PER_ROUND) continue;
+        st_shared_v2(addr_of(f), __float_as_uint(fin[f]), __float_as_uint(fin[f + 1]));
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && rows_in) {
+#pragma unroll
+        for (int bi = 0; bi < PER_ROUND; ++bi) {
+          const int c = col0 + (bx0 + bi) * 32;
+          if (c < p.n) tma_store_3d(&tmap_out, stage_out + bi * 4096, c, tc.m0 + quarter * 32, tc.e);
+        }
+        bulk_commit_group();
+      }
+    }
+  }
+  return true;
 }
 
 // PAIR: a cluster of two CTAs computes a 256 x BN tile with cta_group::2
@@ -640,6 +797,73 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
         // is in flight while chunk c is promoted. Once the last chunk is in
         // registers the TMEM buffer goes back to the MMA warp, before its math.
         constexpr int CH = C::CHUNK;
+        if constexpr (C::FRAG16) {
+          // Chunk c: 8-column groups [c GC, (c + 1) GC) of both 16-row halves of
+          // the warp's lanes, one load per half, one wait; the chunk's column
+          // scales are one 8-byte load per group, shared by both halves.
+          constexpr int GC = C::GC;
+          constexpr int NCH = C::COLS_PER_WARP / (8 * GC);
+          static_assert(GC == 4, "one 16x256b.x4 load per half per chunk");
+          const int rq = lane >> 2;
+#if WGRAD_DEBUG_MODES
+          const float sa4[4] = {unit_scales ? 1.f : sc[quarter * 32 + rq], unit_scales ? 1.f : sc[quarter * 32 + rq + 8],
+                                unit_scales ? 1.f : sc[quarter * 32 + rq + 16],
+                                unit_scales ? 1.f : sc[quarter * 32 + rq + 24]};
+#else
+          const float sa4[4] = {sc[quarter * 32 + rq], sc[quarter * 32 + rq + 8], sc[quarter * 32 + rq + 16],
+                                sc[quarter * 32 + rq + 24]};
+#endif
+          const float* sb_t = b_s + 2 * (lane & 3);
+          uint32_t r[2][8 * GC];
+          tmem_ld_16x256b_x4(t_addr, r[0]);
+          tmem_ld_16x256b_x4(t_addr + (16u << 16), r[0] + 4 * GC);
+#pragma unroll
+          for (int c = 0; c < NCH; ++c) {
+            tmem_wait_ld_bind(r[c & 1]);
+#if WGRAD_TRACE == 2
+            if (ew == 0 && c < 4) WGRAD_TRACE_EV(1 + c, trace_b);
+#endif
+            if (c + 1 < NCH) {
+              tmem_ld_16x256b_x4(t_addr + (c + 1) * 8 * GC, r[(c + 1) & 1]);
+              tmem_ld_16x256b_x4(t_addr + (16u << 16) + (c + 1) * 8 * GC, r[(c + 1) & 1] + 4 * GC);
+            } else {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) {
+                if (PAIR && rank != 0) mbar_arrive_cluster(tempty_addr0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
+                else mbar_arrive(&tempty_bar[acc]);
+              }
+              if (ew == 0) WGRAD_TRACE_EV(WGRAD_TRACE == 2 ? 5 : kTrEpiReleased, trace_b);
+            }
+#pragma unroll
+            for (int g = 0; g < GC; ++g) {
+#if WGRAD_DEBUG_MODES
+              const float2 sb2 = unit_scales ? make_float2(1.f, 1.f)
+                                             : *reinterpret_cast<const float2*>(sb_t + 8 * (c * GC + g));
+#else
+              const float2 sb2 = *reinterpret_cast<const float2*>(sb_t + 8 * (c * GC + g));
+#endif
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t* q = &r[c & 1][h * 4 * GC + 4 * g];
+                float* f = &fin[c * 8 * GC + h * 4 * GC + 4 * g];
+#if WGRAD_DEBUG_MODES
+                const uint32_t one = __float_as_uint(1.f);
+                const float q0 = __uint_as_float(unit_raw ? one : q[0]), q1 = __uint_as_float(unit_raw ? one : q[1]);
+                const float q2 = __uint_as_float(unit_raw ? one : q[2]), q3 = __uint_as_float(unit_raw ? one : q[3]);
+#else
+                const float q0 = __uint_as_float(q[0]), q1 = __uint_as_float(q[1]);
+                const float q2 = __uint_as_float(q[2]), q3 = __uint_as_float(q[3]);
+#endif
+                float u0, u1, u2, u3;
+                mul_f32x2(u0, u1, q0, q1, sb2.x, sb2.y);
+                mul_f32x2(u2, u3, q2, q3, sb2.x, sb2.y);
+                fma_f32x2(f[0], f[1], u0, u1, sa4[2 * h], sa4[2 * h], f[0], f[1]);
+                fma_f32x2(f[2], f[3], u2, u3, sa4[2 * h + 1], sa4[2 * h + 1], f[2], f[3]);
+              }
+            }
+          }
+        } else {
         uint32_t r[2][CH];
         tmem_ld_chunk(t_addr, r[0]);
 #pragma unroll
@@ -679,6 +903,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
             fma_f32x2(f[2], f[3], u2, u3, a_s, a_s, f[2], f[3]);
           }
         }
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sempty_bar[sstage]);
         if (ew == 0) WGRAD_TRACE_EV(WGRAD_TRACE == 2 ? 6 : kTrEpiDone, trace_b);
@@ -699,8 +924,10 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
       if (p.mode == kModeCoordM || p.mode == kModeCoordN || p.mode == kModeScaleOnly) {
 #pragma unroll
         for (int j = 0; j < C::COLS_PER_WARP; ++j) {
-          fin[j] = p.mode == kModeCoordM ? static_cast<float>(g_row)
-                 : p.mode == kModeCoordN ? static_cast<float>(col0 + j)
+          const int jr = C::FRAG16 ? tc.m0 + quarter * 32 + frag_row<C::GC>(j, lane) : g_row;
+          const int jc = C::FRAG16 ? frag_col<C::GC>(j, lane) : j;
+          fin[j] = p.mode == kModeCoordM ? static_cast<float>(jr)
+                 : p.mode == kModeCoordN ? static_cast<float>(col0 + jc)
                                          : fin[j] * 1048576.0f;  // 2^20, as the reference
         }
       }
@@ -710,8 +937,12 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
       if (lane == 0) bulk_wait_group_read0();
       __syncwarp();
       WGRAD_PROF_ADD(kProfEpiStoreWait, ts1);
-      ok = store_warp_tile<C::COLS_PER_WARP, C::OUT_STAGE_BYTES_PER_WARP>(
-          fin, tmap_out, p, tc, quarter, lane, col0, stage_out, &oldout_bar[ew], oldout_phase, abort_flag);
+      if constexpr (C::FRAG16)
+        ok = store_warp_tile_frag<C::COLS_PER_WARP, C::OUT_STAGE_BYTES_PER_WARP, C::GC>(
+            fin, tmap_out, p, tc, quarter, lane, col0, stage_out, &oldout_bar[ew], oldout_phase, abort_flag);
+      else
+        ok = store_warp_tile<C::COLS_PER_WARP, C::OUT_STAGE_BYTES_PER_WARP>(
+            fin, tmap_out, p, tc, quarter, lane, col0, stage_out, &oldout_bar[ew], oldout_phase, abort_flag);
       if (!ok) break;
       WGRAD_PROF_ADD(kProfEpiStore, ts0);
     }
