@@ -468,8 +468,8 @@ def run_ours(args) -> None:
         f"setup {time.perf_counter() - t_setup:.1f}s")
 
     def step():
-        run_custom_down(inp)
-        run_custom_gate_up(inp)
+        run_custom_down(inp, tuned_config=args.tuned_config)
+        run_custom_gate_up(inp, tuned_config=args.tuned_config)
 
     for _ in range(args.warmup):
         step()
@@ -485,9 +485,9 @@ def run_ours(args) -> None:
     clocks.start()
     for s in range(args.steps):
         evs[s][0].record(stream)
-        run_custom_down(inp)
+        run_custom_down(inp, tuned_config=args.tuned_config)
         evs[s][1].record(stream)
-        run_custom_gate_up(inp)
+        run_custom_gate_up(inp, tuned_config=args.tuned_config)
         evs[s][2].record(stream)
     torch.cuda.synchronize(dev)
     clk = clocks.stop()
@@ -570,7 +570,7 @@ def run_ours(args) -> None:
             "vs_baseline_ref": "published reference sm90 kernel figure on H100, same per-GPU problem",
             "dtype": "fp8e4m3->f32acc->bf16",
             "data": "synthetic",
-            "config": workload_config(args.workload, world, args.layout, args.scale_format),
+            "config": dict(workload_config(args.workload, world, args.layout, args.scale_format), tuned_config=args.tuned_config),
             "stages_ms": {"down": down_ms, "gate_up": gate_ms},
             "stages_tflops": {"down": down_flops_tf, "gate_up": gate_flops_tf},
             "pct_of_fp8_peak": value / world / fp8_peak,
@@ -668,7 +668,7 @@ def run_e2e(inp, args, world, dev, step_flops) -> dict:
             for c, (e0, e1) in enumerate(chunks):
                 s_cmp.wait_event(ev_out[g][c])         # the previous copy-out of this chunk is done
                 with torch.cuda.stream(s_cmp):
-                    fp8_grouped_wgrad_sm90(lhs, rhs, out, m, expert_range=(e0, e1))
+                    fp8_grouped_wgrad_sm90(lhs, rhs, out, m, expert_range=(e0, e1), tuned_config=args.tuned_config)
                 ev_cmp[g][c].record(s_cmp)
                 s_d2h.wait_event(ev_cmp[g][c])
                 with torch.cuda.stream(s_d2h):
@@ -717,6 +717,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tuned-config", default="default",
+                    help="tuned_config passed to fp8_grouped_wgrad_sm90 (default: the library's automatic choice)")
     ap.add_argument("--no-library-rate", action="store_true",
                     help="skip the cuBLAS FP8 GEMM rate measured after the timed region (about 5 s)")
     args = ap.parse_args()

@@ -54,9 +54,12 @@ extern "C" {
 #define SM100_WGRAD_OUT_F32 1
 
 /* Tile configurations selectable through Sm100WgradArgs.tile_config.
- * AUTO picks the N width by shape; AUTO and 128x256 pick the number of
- * promotion warps of the 256-wide tile by K depth (16 when the experts average
- * few 128-row blocks, 8 otherwise); the _W8 / _W16 forms force it. */
+ * AUTO picks the 256x256 CTA pair (below) when the experts average at least
+ * 8 128-row blocks and each expert has at least 64 256x256 output tiles, and
+ * a single-CTA tile otherwise, its N width by shape; AUTO and 128x256 pick the
+ * number of promotion warps of the 256-wide single-CTA tile by K depth (16
+ * when the experts average few 128-row blocks, 8 otherwise); the _W8 / _W16
+ * forms force it. */
 #define SM100_WGRAD_TILE_AUTO 0
 #define SM100_WGRAD_TILE_128x256 1
 #define SM100_WGRAD_TILE_128x128 2
