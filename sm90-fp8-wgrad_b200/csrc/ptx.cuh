@@ -393,6 +393,12 @@ __device__ __forceinline__ void tmem_ld_16x256b_x4(uint32_t taddr, uint32_t* r) 
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
 // Shared memory -> TMEM copy of a 32-row x 128-bit matrix, replicated into all
 // four lane quarters (tcgen05.cp 32x128b.warpx4): row r lands in lane
 // 32 q + r of every quarter q, its 16 bytes in columns [taddr.col, +4).

@@ -144,7 +144,7 @@ struct Cfg {
   // Promotion in the 16x256b fragment layout (two rows and a column pair per
   // thread): 8-byte column-scale loads shared by 8 lanes' rows instead of a
   // 16-byte broadcast per 4 columns, a quarter of the shared-memory wavefronts.
-  static constexpr bool FRAG16 = WGRAD_FRAG16 != 0 && EPI_WARPS == 8 && BN == 256;
+  static constexpr bool FRAG16 = WGRAD_FRAG16 != 0 && (EPI_WARPS == 8 || EPI_WARPS == 16) && BN == 256;
   static constexpr int GC = CHUNK / 8;  // 8-column groups per chunk of the fragment layout
   static constexpr int CHUNKS = COLS_PER_WARP / CHUNK;
   static constexpr int OUT_STAGE_BYTES_PER_WARP =
@@ -803,7 +803,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
           // scales are one 8-byte load per group, shared by both halves.
           constexpr int GC = C::GC;
           constexpr int NCH = C::COLS_PER_WARP / (8 * GC);
-          static_assert(GC == 4, "one 16x256b.x4 load per half per chunk");
+          static_assert(GC == 4 || GC == 2, "one 16x256b.x4 or .x2 load per half per chunk");
           const int rq = lane >> 2;
 #if WGRAD_DEBUG_MODES
           const float sa4[4] = {unit_scales ? 1.f : sc[quarter * 32 + rq], unit_scales ? 1.f : sc[quarter * 32 + rq + 8],
@@ -815,8 +815,12 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
 #endif
           const float* sb_t = b_s + 2 * (lane & 3);
           uint32_t r[2][8 * GC];
-          tmem_ld_16x256b_x4(t_addr, r[0]);
-          tmem_ld_16x256b_x4(t_addr + (16u << 16), r[0] + 4 * GC);
+          auto ld_half = [](uint32_t addr, uint32_t* dst) {
+            if constexpr (GC == 4) tmem_ld_16x256b_x4(addr, dst);
+            else tmem_ld_16x256b_x2(addr, dst);
+          };
+          ld_half(t_addr, r[0]);
+          ld_half(t_addr + (16u << 16), r[0] + 4 * GC);
 #pragma unroll
           for (int c = 0; c < NCH; ++c) {
             tmem_wait_ld_bind(r[c & 1]);
@@ -824,8 +828,8 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
             if (ew == 0 && c < 4) WGRAD_TRACE_EV(1 + c, trace_b);
 #endif
             if (c + 1 < NCH) {
-              tmem_ld_16x256b_x4(t_addr + (c + 1) * 8 * GC, r[(c + 1) & 1]);
-              tmem_ld_16x256b_x4(t_addr + (16u << 16) + (c + 1) * 8 * GC, r[(c + 1) & 1] + 4 * GC);
+              ld_half(t_addr + (c + 1) * 8 * GC, r[(c + 1) & 1]);
+              ld_half(t_addr + (16u << 16) + (c + 1) * 8 * GC, r[(c + 1) & 1] + 4 * GC);
             } else {
               tc_fence_before();
               __syncwarp();
