@@ -188,8 +188,9 @@ def test_grouped_wgrad_fp32_out_and_accumulate(cuda_device, tuned_config):
     np.testing.assert_allclose(got, expect, rtol=2 ** -7, atol=1e-5 * float(np.abs(expect).max()))
 
 
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_128x192_w12",
-                                          "sm100_256x256_pair", "sm100_256x256_sp", "sm100_256x256_sp_w16"])
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w8", "sm100_128x256_w16", "sm100_128x128_2cta",
+                                          "sm100_128x192_w12", "sm100_256x256_pair", "sm100_256x256_pair_w16",
+                                          "sm100_256x256_sp", "sm100_256x256_sp_w16"])
 @pytest.mark.parametrize("hidden,inter", [(144, 80), (272, 48), (512, 128)])
 def test_grouped_wgrad_ragged_tiles(cuda_device, hidden, inter, tuned_config):
     """M, N not multiples of the 128 x 256 tile; empty experts; long K."""
@@ -246,7 +247,8 @@ def test_expert_range_launches_equal_full_launch(cuda_device, splits, tuned_conf
 
 
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w16", "sm100_128x128_2cta", "sm100_128x192_w12",
+@pytest.mark.parametrize("tuned_config", ["default", "sm100_128x256_w8", "sm100_128x256_w16", "sm100_128x128_2cta",
+                                          "sm100_128x192_w12", "sm100_256x256_pair", "sm100_256x256_pair_w16",
                                           "sm100_256x256_sp", "sm100_256x256_sp_w16"])
 def test_accumulate_on_ragged_tiles(cuda_device, tuned_config, out_dtype):
     """out += result where M, N are not multiples of the tile (the previous output
