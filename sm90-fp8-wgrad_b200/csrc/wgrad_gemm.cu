@@ -868,45 +868,45 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
             }
           }
         } else {
-        uint32_t r[2][CH];
-        tmem_ld_chunk(t_addr, r[0]);
+          uint32_t r[2][CH];
+          tmem_ld_chunk(t_addr, r[0]);
 #pragma unroll
-        for (int c = 0; c < C::CHUNKS; ++c) {
-          tmem_wait_ld_bind(r[c & 1]);
+          for (int c = 0; c < C::CHUNKS; ++c) {
+            tmem_wait_ld_bind(r[c & 1]);
 #if WGRAD_TRACE == 2
-          if (ew == 0 && c < 4) WGRAD_TRACE_EV(1 + c, trace_b);
+            if (ew == 0 && c < 4) WGRAD_TRACE_EV(1 + c, trace_b);
 #endif
-          if (c + 1 < C::CHUNKS) {
-            tmem_ld_chunk(t_addr + (c + 1) * CH, r[(c + 1) & 1]);
-          } else {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-              if (PAIR && rank != 0) mbar_arrive_cluster(tempty_addr0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
-              else mbar_arrive(&tempty_bar[acc]);
+            if (c + 1 < C::CHUNKS) {
+              tmem_ld_chunk(t_addr + (c + 1) * CH, r[(c + 1) & 1]);
+            } else {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) {
+                if (PAIR && rank != 0) mbar_arrive_cluster(tempty_addr0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
+                else mbar_arrive(&tempty_bar[acc]);
+              }
+              if (ew == 0) WGRAD_TRACE_EV(WGRAD_TRACE == 2 ? 5 : kTrEpiReleased, trace_b);
             }
-            if (ew == 0) WGRAD_TRACE_EV(WGRAD_TRACE == 2 ? 5 : kTrEpiReleased, trace_b);
-          }
 #pragma unroll
-          for (int j = 0; j < CH; j += 4) {
+            for (int j = 0; j < CH; j += 4) {
 #if WGRAD_DEBUG_MODES
-            const float4 sb4 = unit_scales ? make_float4(1.f, 1.f, 1.f, 1.f)
-                                           : *reinterpret_cast<const float4*>(b_s + c * CH + j);
-            const uint32_t one = __float_as_uint(1.f);
-            const uint32_t q[4] = {unit_raw ? one : r[c & 1][j], unit_raw ? one : r[c & 1][j + 1],
-                                   unit_raw ? one : r[c & 1][j + 2], unit_raw ? one : r[c & 1][j + 3]};
+              const float4 sb4 = unit_scales ? make_float4(1.f, 1.f, 1.f, 1.f)
+                                             : *reinterpret_cast<const float4*>(b_s + c * CH + j);
+              const uint32_t one = __float_as_uint(1.f);
+              const uint32_t q[4] = {unit_raw ? one : r[c & 1][j], unit_raw ? one : r[c & 1][j + 1],
+                                     unit_raw ? one : r[c & 1][j + 2], unit_raw ? one : r[c & 1][j + 3]};
 #else
-            const float4 sb4 = *reinterpret_cast<const float4*>(b_s + c * CH + j);
-            const uint32_t* q = &r[c & 1][j];
+              const float4 sb4 = *reinterpret_cast<const float4*>(b_s + c * CH + j);
+              const uint32_t* q = &r[c & 1][j];
 #endif
-            float u0, u1, u2, u3;
-            mul_f32x2(u0, u1, __uint_as_float(q[0]), __uint_as_float(q[1]), sb4.x, sb4.y);
-            mul_f32x2(u2, u3, __uint_as_float(q[2]), __uint_as_float(q[3]), sb4.z, sb4.w);
-            float* f = &fin[c * CH + j];
-            fma_f32x2(f[0], f[1], u0, u1, a_s, a_s, f[0], f[1]);
-            fma_f32x2(f[2], f[3], u2, u3, a_s, a_s, f[2], f[3]);
+              float u0, u1, u2, u3;
+              mul_f32x2(u0, u1, __uint_as_float(q[0]), __uint_as_float(q[1]), sb4.x, sb4.y);
+              mul_f32x2(u2, u3, __uint_as_float(q[2]), __uint_as_float(q[3]), sb4.z, sb4.w);
+              float* f = &fin[c * CH + j];
+              fma_f32x2(f[0], f[1], u0, u1, a_s, a_s, f[0], f[1]);
+              fma_f32x2(f[2], f[3], u2, u3, a_s, a_s, f[2], f[3]);
+            }
           }
-        }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sempty_bar[sstage]);
