@@ -29,6 +29,9 @@ from .quant import (
 # onto the B200 tile shapes. The SM90 cluster/pingpong variants have no
 # separate meaning on tcgen05: every name resolves to the persistent kernel
 # with a 128-row tile and the N width listed here (0 = choose by shape).
+# Tile configs whose kernel needs a workspace (sm100_wgrad_workspace_bytes > 0).
+_SP_TILES = frozenset((_lib.TILE_256x256_SP, _lib.TILE_256x256_SP_W16))
+
 TUNED_CONFIGS: dict[str, int] = {
     "default": _lib.TILE_AUTO,
     "optB_coop128_default": _lib.TILE_AUTO,
@@ -299,22 +302,39 @@ def fp8_grouped_wgrad_sm90(
     args.tile_config = TUNED_CONFIGS[resolved]
     args.max_ctas = int(os.environ.get("SM100_WGRAD_MAX_CTAS", "0") or 0)
     lib = _lib.load()
-    with torch.cuda.device(dev):
-        # A device-side failure of an earlier launch (bounded wait that gave up,
-        # mislabelled UE8M0 scales, bad gather index) surfaces here, without a sync.
-        _lib.raise_pending_device_error()
-    need = ctypes.c_int64(0)
-    _lib.check(lib.sm100_wgrad_workspace_bytes(ctypes.byref(args), ctypes.byref(need)), "sm100_wgrad_workspace_bytes")
-    workspace = None
-    if need.value > 0:
-        # Scratch for the split scales, from the caching allocator on the
-        # launch stream; it is released when the launch has consumed it.
-        workspace = torch.empty(int(need.value), dtype=torch.uint8, device=dev)
-        args.workspace, args.workspace_bytes = workspace.data_ptr(), int(need.value)
-    with torch.cuda.device(dev):
-        status = lib.sm100_fp8_grouped_wgrad(ctypes.byref(args), torch.cuda.current_stream().cuda_stream)
+    if torch.cuda.current_device() == dev.index:
+        status = _launch(lib, args, dev)
+    else:
+        with torch.cuda.device(dev):
+            status = _launch(lib, args, dev)
     _lib.check(status, "sm100_fp8_grouped_wgrad")
     return out
+
+
+def _current_stream_handle(index: int) -> int:
+    """Raw cudaStream_t of the device's current stream (the cheap accessor
+    where this torch has it)."""
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    return raw(index) if raw is not None else torch.cuda.current_stream(index).cuda_stream
+
+
+def _launch(lib, args, dev: torch.device) -> int:
+    """The C-ABI call, with ``dev`` current: first surface a device-side failure
+    of an earlier launch (bounded wait that gave up, mislabelled UE8M0 scales,
+    bad gather index) without a sync, then size the workspace (only the
+    scale-product configs have one), then launch on the current stream."""
+    _lib.raise_pending_device_error()
+    workspace = None
+    if args.tile_config in _SP_TILES:
+        need = ctypes.c_int64(0)
+        _lib.check(lib.sm100_wgrad_workspace_bytes(ctypes.byref(args), ctypes.byref(need)),
+                   "sm100_wgrad_workspace_bytes")
+        if need.value > 0:
+            # Scratch for the split scales, from the caching allocator on the
+            # launch stream; it is released when the launch has consumed it.
+            workspace = torch.empty(int(need.value), dtype=torch.uint8, device=dev)
+            args.workspace, args.workspace_bytes = workspace.data_ptr(), int(need.value)
+    return lib.sm100_fp8_grouped_wgrad(ctypes.byref(args), _current_stream_handle(dev.index))
 
 
 # B200-native alias of the same operator.
