@@ -767,11 +767,14 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::THREADS, Cfg<BN, EPI, PAIR
     int trace_b = 0;
     for (int r = 0, tile = tile_begin; r * tile_stride < p.num_tiles && ok; tile = sched_tile<PAIR>(++r, tile_begin, tile_stride)) {
     if (tile >= p.num_tiles) continue;
+      // trace 1: tile start and tile decoded, in the slots the scale-product kernel uses for its second half
+      if (ew == 0 && WGRAD_TRACE == 1) WGRAD_TRACE_EV(kTrMmaHalfReady, trace_b);
       const TileCoord tc = decode_tile(p, tile, row_off);
       const int nkb = __ldg(p.block_offsets + tc.e + 1) - __ldg(p.block_offsets + tc.e);
       float fin[C::COLS_PER_WARP];
 #pragma unroll
       for (int j = 0; j < C::COLS_PER_WARP; ++j) fin[j] = 0.f;
+      if (ew == 0 && WGRAD_TRACE == 1 && nkb > 0) WGRAD_TRACE_EV(kTrMmaHalfIssued, trace_b);
 
       for (int kb = 0; kb < nkb; ++kb, ++trace_b) {
         if (ew == 0) WGRAD_TRACE_EV(WGRAD_TRACE == 2 ? 7 : kTrEpiWaitStart, trace_b);

@@ -11,7 +11,8 @@ One warm gate_up launch, then one traced launch; prints, for CTA 0 (and its
 pair peer, CTA 1), the SM clock64 stamps of the first 40 K blocks relative to
 the earliest stamp. Trace 1: MMA issuer ready / issued, promotion warp wait
 start / partial ready / buffer released / block done (scale-product kernel:
-ready/issued of its second half in the last two columns). Trace 2: promotion
+ready/issued of its second half in the last two columns; promotion kernels:
+tile start and tile decoded, on the first block of each tile). Trace 2: promotion
 warp ready, chunks 0-3 in registers, released, done, next wait start.
 """
 from __future__ import annotations
