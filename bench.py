@@ -515,7 +515,7 @@ def run_ours(args) -> None:
     gate_flops_tf = f_gate / (gate_ms * 1e-3) / 1e12
     down_flops_tf = f_down / (down_ms * 1e-3) / 1e12
     kname = ("grouped_wgrad_ue8m0_kernel (gate_up launch)" if args.scale_format == "ue8m0"
-             else "grouped_wgrad_kernel<256> (gate_up launch)")
+             else "grouped_wgrad_kernel, AUTO tile (gate_up launch)")
     if bound == "tensor":
         roof = {"bound": "tensor", "kernel": kname,
                 "achieved": gate_flops_tf, "peak": fp8_peak, "unit": "TFLOP/s", "frac": gate_flops_tf / fp8_peak,
